@@ -1,0 +1,348 @@
+#!/usr/bin/env python
+"""Benchmark of the hot path: the whole FastDEC fit (exact self-kNN -> density -> DC detection ->
+DC reduction -> labels) on the headline workload, 1,291,147 x 50 fp32, k=45, c=20 (
+a seeded synthetic stand-in for GloVe 50d).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0). Metric: unordered distance pairs per second of the whole fit,
+N(N-1)/2 per fit -- the reference's work unit (8.3353e11 pairs for this workload).
+  value       fits with the dataset already resident in HBM (device pointers, the fit's own stream)
+  e2e         the same fits through the public host-pointer API: pinned host data in, labels and
+              centers out, host<->device copies inside the timed region
+  roofline    the distance-tile kernels (the dominant kernel), timed live with CUDA events
+  cpu_baseline  the reference's host Fit stages (oracle/_ref, compiled from the reference sources)
+              with CPU kNN / DC-reduction stand-ins, on a bounded sample, all host cores
+With N > 1 (torchrun), every rank computes its share of the triangle into partial per-point lists,
+an NCCL all-to-all sends each list to its owner rank, owners merge, rank 0 gathers the merged
+lists and finishes the fit. Timing is the max over ranks of device time (CUDA events).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "symwarp-fastdec_b200"))
+
+PUBLISHED_A6000_FIT_S = 16.49          # README.md:149, symwarp FP32 Fit seconds on GloVe 50d (A6000)
+WORKLOAD = dict(n=1_291_147, d=50, k=45, c=20)
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=3)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--n", type=int, default=WORKLOAD["n"])
+    p.add_argument("--d", type=int, default=WORKLOAD["d"])
+    p.add_argument("--k", type=int, default=WORKLOAD["k"])
+    p.add_argument("--c", type=int, default=WORKLOAD["c"])
+    p.add_argument("--precision", default="fp32", choices=["fp32", "tf32"])
+    p.add_argument("--density", default="laplacian", choices=["laplacian", "gaussian"])
+    p.add_argument("--engine", default="auto", choices=["auto", "simt", "tcgen05"])
+    p.add_argument("--seed", type=int, default=3)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=8.0, help="target CPU seconds per reference sample")
+    return p.parse_args()
+
+
+def dataset(a):
+    from fastdec_b200.datasets import embedding_cloud
+    return embedding_cloud(n=a.n, d=a.d, seed=a.seed)
+
+
+def pairs_of(n):
+    return n * (n - 1) // 2
+
+
+def config_of(a, extra=None):
+    c = {"workload": f"glove_like {a.n:,} x {a.d}, k={a.k}, c={a.c}, {a.precision.upper()} distances, "
+                     f"{a.density} density",
+         "n": a.n, "d": a.d, "k": a.k, "c": a.c, "precision": a.precision, "density": a.density,
+         "engine": a.engine, "seed": a.seed, "parallelism": f"triangle-sharded x{a.gpus}",
+         "l2": "inputs larger than L2 (258 MB dataset, 465 MB lists per fit; no flush needed)"}
+    if extra:
+        c.update(extra)
+    return c
+
+
+DATA_NOTE = ("synthetic: seeded stand-in for GloVe 50d (20 anisotropic Gaussians, Zipf(1.1) weights, "
+             "5% Student-t(3) points, min-max scaled to [-1,1])")
+
+
+# ------------------------------------------------------------------ clocks during the timed region
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = str(gpu_index)
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9 and parts[0] == self.gpu:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = [nm for i, nm in enumerate(names) if any(r[5 + i].lower().startswith("active") for r in self.rows)]
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def physical_gpu(local):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local < len(ids) and ids[local].isdigit():
+            return int(ids[local])
+    return local
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return j.get("bf16_tflops", 1590.0), j.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ CPU reference (oracle/_ref)
+def run_reference_sample(x_full, a, target_s, steps=1, warmup=0):
+    """Times the reference's host Fit (oracle/_ref) on a prefix sample of the (shuffled) dataset."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("FASTDEC_DENSITY_THREADS", "0")
+    os.environ.setdefault("FASTDEC_ORACLE_THREADS", str(cores))
+    use_ref = oracle.ref_available(a.density == "gaussian")
+    runner = (lambda x: oracle.ref_fit(x, a.k, a.c, gaussian=a.density == "gaussian")) if use_ref else \
+             (lambda x: oracle.fit(x, a.k, a.c, gaussian=a.density == "gaussian", nthreads=cores))
+    # calibrate the sample size on a small prefix (the kNN is O(n^2) and dominates)
+    n0 = min(a.n, 8000)
+    t0 = time.perf_counter()
+    runner(np.ascontiguousarray(x_full[:, :n0]))
+    dt = max(time.perf_counter() - t0, 1e-3)
+    rate = pairs_of(n0) / dt
+    ns = int(min(a.n, max(n0, (2 * target_s * rate) ** 0.5)))
+    xs = np.ascontiguousarray(x_full[:, :ns])
+    for _ in range(warmup):
+        runner(xs)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        runner(xs)
+        times.append(time.perf_counter() - t0)
+    mean_s = float(np.mean(times))
+    kind = "reference" if use_ref else "port"
+    sample = (f"first {ns:,} of the {a.n:,} shuffled points (d={a.d}, k={a.k}, c={a.c}); "
+              + ("reference FastDECBase::Fit host stages compiled from source (oracle/_ref) with the oracle's "
+                 "multithreaded exact CPU kNN and DC reduction standing in for its GPU calls"
+                 if use_ref else "oracle CPU restatement of the whole fit"))
+    return dict(value=pairs_of(ns) / mean_s, unit="pairs/s", cores=cores, kind=kind, sample=sample,
+                seconds_per_fit=mean_s, n_sample=ns)
+
+
+# ------------------------------------------------------------------ our engine
+def main():
+    a = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    a.gpus = world if world > 1 else a.gpus
+
+    if a.impl == "reference":
+        if rank != 0:
+            return 0
+        x = dataset(a)
+        ref = run_reference_sample(x, a, a.cpu_seconds, steps=a.steps, warmup=a.warmup)
+        out = {"impl": "reference", "metric": "fit_distance_pairs_per_s", "value": ref["value"], "unit": "pairs/s",
+               "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ref["seconds_per_fit"] * 1e3,
+               "higher_is_better": True, "scaling": "strong",
+               "vs_baseline": ref["value"] / (pairs_of(WORKLOAD["n"]) / PUBLISHED_A6000_FIT_S),
+               "dtype": "f32", "data": DATA_NOTE, "config": config_of(a, {"sample_points": ref["n_sample"]}),
+               "cpu_baseline": {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
+               "e2e": {"value": ref["value"], "unit": "pairs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(out), flush=True)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+    import fastdec_b200 as fdb
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    fdb.lib()
+
+    x_host = dataset(a)
+    n, d, k, c = a.n, a.d, a.k, a.c
+    x_dev = torch.from_numpy(x_host).to(dev)
+    centers = torch.empty(c, dtype=torch.int32, device=dev)
+    labels = torch.empty(n, dtype=torch.int32, device=dev)
+    kw = dict(precision=a.precision, density=a.density, engine=a.engine)
+
+    if world > 1:
+        from fastdec_b200.multigpu import ShardedFit
+        runner = ShardedFit(n, d, k, c, rank, world, dev, sp, **kw)
+
+        def step():
+            return runner.step(x_dev, centers, labels)
+    else:
+        def step():
+            return fdb.fit_device(x_dev, k, c, centers, labels, stream=sp, **kw)
+
+    for _ in range(a.warmup):
+        st = step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stats = []
+    with ClockSampler(physical_gpu(local)) as clk:
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        ev0.record(stream)
+        for _ in range(a.steps):
+            stats.append(step())
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / a.steps
+    value = pairs_of(n) / (ms_step / 1e3)
+    launches = int(sum(s.get("launches", 0) for s in stats))
+    tile_ms = float(np.mean([s.get("knn_tile_ms", 0.0) for s in stats]))
+    rounds = float(np.mean([s.get("rounds", 0) for s in stats]))
+    shard_pairs = float(np.mean([s.get("pairs", 0) for s in stats]))
+
+    # e2e through the public host-pointer API: pinned host input, labels + centers back to the host
+    e2e = None
+    if not a.no_e2e:
+        pinned = torch.empty((d, n), dtype=torch.float32, pin_memory=True)
+        pinned.numpy()[...] = x_host
+        lab_h = torch.empty(n, dtype=torch.int32, pin_memory=True)
+        ctr_h = torch.empty(c, dtype=torch.int32, pin_memory=True)
+        if world > 1:
+            def e2e_step():
+                xd = pinned.to(dev, non_blocking=True)
+                runner.step(xd, centers, labels)
+                if rank == 0:
+                    lab_h.copy_(labels, non_blocking=True)
+                    ctr_h.copy_(centers, non_blocking=True)
+        else:
+            from fastdec_b200 import _ptr, make_opts, lib, Stats, _check
+            import ctypes
+
+            def e2e_step():
+                st = Stats()
+                _check(lib().fdb200_fit(_ptr(pinned), n, d, k, c, ctypes.byref(make_opts(stream=sp, **kw)),
+                                        _ptr(ctr_h), _ptr(lab_h), None, ctypes.byref(st)))
+        e2e_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(a.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ems = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ems], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        e2e = {"value": pairs_of(n) / (ems / a.steps / 1e3), "unit": "pairs/s",
+               "h2d_bytes_per_step": n * d * 4 * world, "d2h_bytes_per_step": (n + c) * 4,
+               "ms_per_step": ems / a.steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        ref = run_reference_sample(x_host, a, a.cpu_seconds)
+        cpu = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    if world > 1:
+        dist.barrier()
+        runner.close()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    bf16, hbm, src = measured_peaks()
+    tf32_peak = bf16 / 2.0
+    flops = shard_pairs * 2 * d
+    achieved = flops / (tile_ms / 1e3) / 1e12 if tile_ms > 0 else None
+    roofline = {"bound": "tensor", "kernel": "distance tiles (knn_tile_*)",
+                "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
+                "frac": (achieved / tf32_peak) if achieved else None, "traffic": None,
+                "peak_note": f"dense TF32 = 1/2 of the {src} bf16 burst figure ({bf16} TF/s)",
+                "launches_per_fit": rounds, "algorithmic_flops_per_fit": flops}
+    last = stats[-1]
+    out = {"metric": "fit_distance_pairs_per_s", "value": value, "unit": "pairs/s", "n_gpus": world,
+           "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": value / (pairs_of(WORKLOAD["n"]) / PUBLISHED_A6000_FIT_S),
+           "dtype": "f32" if a.precision == "fp32" else "tf32", "data": DATA_NOTE, "config": config_of(a),
+           "fit_s": ms_step / 1e3, "knn_s": last.get("knn_ms", 0) / 1e3,
+           "stages_ms": {k2: last.get(k2) for k2 in ("knn_ms", "knn_tile_ms", "density_ms", "dc_ms", "labels_ms")},
+           "rounds": last.get("rounds"), "num_cores": last.get("num_cores"), "final_k": last.get("final_k"),
+           "engine_used": {1: "simt", 2: "tcgen05"}.get(last.get("engine_used"), "?"),
+           "centers": centers.cpu().tolist(), "gpu_launches": launches, "clocks": clk.summary(),
+           "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+           "vs_baseline_note": "value / (8.3353e11 pairs / 16.49 s): the reference's published symwarp FP32 "
+                               "Fit on GloVe 50d, RTX A6000 (README.md:149)"}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

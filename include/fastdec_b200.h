@@ -1,0 +1,175 @@
+/*
+ * fastdec_b200.h -- C ABI of the B200 FastDEC engine (libfastdec_b200.so).
+ *
+ * Plain pointers and sizes only; no exceptions cross this boundary. Every call returns
+ * FDB200_OK (0) or a negative FDB200_E* code; fdb200_last_error() gives the message for the
+ * calling thread's last failure. Each entry point names the reference interface it replaces
+ * (paths inside cyberbull66/symwarp-fastdec).
+ *
+ * Data layout is the reference's: the dataset is DIM-MAJOR, element (dim t, point i) at
+ * data[t * n + i] (test.cpp:110-115, dataset.h:8-39). kNN outputs are RANK-MAJOR, element
+ * (point i, rank q) at [q * n + i] (symtriknncuda.h:11-12, helper.cpp:295-317).
+ *
+ * Pointers are host pointers unless FdB200Opts.inputs_on_device / outputs_on_device say they
+ * are device pointers on FdB200Opts.device.
+ */
+#ifndef FASTDEC_B200_H
+#define FASTDEC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FDB200_ABI_VERSION 1
+
+enum {
+    FDB200_OK = 0,
+    FDB200_EINVAL = -1,      /* bad argument (the reference returns false / throws) */
+    FDB200_ECUDA = -2,       /* a CUDA runtime call failed */
+    FDB200_ENOMEM = -3,      /* device allocation failed */
+    FDB200_ECORES = -4,      /* "Fit: not enough core points" (fastdecbase.cpp:188-191) */
+    FDB200_ECYCLE = -5,      /* label propagation did not converge (symwarpfastdeccuda.cu:338-339) */
+    FDB200_EINTERNAL = -6    /* an internal consistency check failed */
+};
+
+enum { FDB200_FP32 = 0, FDB200_TF32 = 1 };              /* distance precision */
+enum { FDB200_LAPLACIAN = 0, FDB200_GAUSSIAN = 1 };    /* density kernel (USE_GAUSSIAN_KERNEL) */
+enum { FDB200_ENGINE_AUTO = 0, FDB200_ENGINE_SIMT = 1, FDB200_ENGINE_TCGEN05 = 2 };
+
+typedef struct FdB200Opts {
+    int struct_size;          /* sizeof(FdB200Opts); set by fdb200_opts_init */
+    int device;               /* CUDA device ordinal (Dataset::cuda_device_id, dataset.h:30) */
+    int precision;            /* FDB200_FP32: distances bit-identical to the reference FDS build
+                                 (fmaf chain); FDB200_TF32: tensor-core TF32 distances */
+    int density_kernel;       /* FDB200_LAPLACIAN (default) or FDB200_GAUSSIAN */
+    int engine;               /* which distance-tile engine runs the self-kNN */
+    int inputs_on_device;     /* nonzero: data / density / index inputs are device pointers */
+    int outputs_on_device;    /* nonzero: outputs are device pointers */
+    int shard_rank;           /* kNN triangle sharding: this shard's index ... */
+    int shard_count;          /* ... out of shard_count (1 = whole triangle) */
+    int cand_capacity;        /* per-point candidate slots per round (0 = automatic) */
+    void* stream;             /* cudaStream_t to run on; NULL = the library's own stream */
+} FdB200Opts;
+
+typedef struct FdB200Stats {
+    double total_ms;          /* device time of the whole call (CUDA events) */
+    double upload_ms;         /* host->device copy of the dataset */
+    double knn_ms;            /* self-kNN (tiles + merges + final ordering) */
+    double density_ms;        /* density + DC detection, including k-halving retries */
+    double dc_ms;             /* DC reduction + center selection */
+    double labels_ms;         /* label propagation + device->host copies */
+    double knn_tile_ms;       /* part of knn_ms spent in the distance-tile kernels */
+    long long pairs;          /* unordered pairs evaluated by this shard */
+    long long candidates;     /* candidates appended to the per-point lists */
+    int rounds;               /* tile rounds run (including overflow re-runs) */
+    int overflow_reruns;      /* rounds re-run because a candidate buffer overflowed */
+    int num_cores;            /* density cores after the k-halving loop */
+    int final_k;              /* k after the k-halving loop */
+    int engine_used;          /* FDB200_ENGINE_SIMT or FDB200_ENGINE_TCGEN05 */
+    int launches;             /* kernels this call launched */
+    int reserved[6];
+} FdB200Stats;
+
+/* Fills opts with defaults (device 0, FP32, Laplacian, auto engine, host pointers, 1 shard). */
+int fdb200_opts_init(FdB200Opts* opts);
+
+/* Message of the calling thread's last failure ("" if none). */
+const char* fdb200_last_error(void);
+
+int fdb200_abi_version(void);
+
+/*
+ * Exact self-kNN: for every point the k nearest other points, ordered by (d2, index), with
+ * Euclidean distances. Replaces symtri_knn_cuda (symtriknncuda.h:15-18) as called through the
+ * kNN plug-in FastDECBase::compute_knn (fastdecbase.h:43-46, symwarpfastdec.cpp:4-10).
+ * out_dist / out_idx: k * n each, rank-major. n <= 1 or k <= 0 is a no-op success; k >= n is
+ * FDB200_EINVAL (symtriknncuda.cu:319-324).
+ */
+int fdb200_knn(const float* data, int n, int d, int k, const FdB200Opts* opts,
+               float* out_dist, int* out_idx, FdB200Stats* stats);
+
+/*
+ * The whole FastDEC fit: self-kNN -> density -> DC detection (with the k-halving retry) ->
+ * DC reduction + center selection -> labels. Replaces FastDECBase::Fit (fastdecbase.h:38,
+ * fastdecbase.cpp:159-228) with get_center_indices() / get_labels() (fastdecbase.h:35-37), and
+ * SymWarpFullGpuFastDEC::Fit (full_gpu/symwarpfullgpufastdec.h:39).
+ * centers_out: c entries; labels_out: n entries; densities_out (optional, may be NULL): n.
+ */
+int fdb200_fit(const float* data, int n, int d, int k, int c, const FdB200Opts* opts,
+               int* centers_out, int* labels_out, float* densities_out, FdB200Stats* stats);
+
+/*
+ * DC reduction + center selection for given cores. Replaces warp_parallel_dc_reduction_cuda
+ * (dcreductioncuda.h:45-51): core_parent_out[i] = nearest strictly denser point of core i
+ * (-1 if none); centers_out: num_centers global indices (-1 padded).
+ */
+int fdb200_dc_reduction(const float* data, int n, int d, const float* densities,
+                        const int* core_indices, int core_nb, int num_centers,
+                        const FdB200Opts* opts, int* core_parent_out, int* centers_out);
+
+/*
+ * Density of every point from the first k ranks of a rank-major kNN distance list whose rank
+ * stride is n. Replaces FastDECBase::density_estimation_{laplacian,gaussian}
+ * (fastdecbase.cpp:276-301; mean as the sequential double sum of fastdecbase.cpp:257-274) and
+ * gpu_density_estimation_* (full_gpu/symwarpfastdeccuda.h:54-58). mean_out may be NULL.
+ */
+int fdb200_density(const float* knn_dist, int n, int k, const FdB200Opts* opts,
+                   float* densities_out, double* mean_out);
+
+/*
+ * DC detection: parent_out[i] = first neighbour (rank order, first k ranks) with a strictly
+ * greater density, else -1; cores_out = points with parent -1 in ascending order (capacity n).
+ * Replaces FastDECBase::dc_detection (fastdecbase.cpp:303-333) / gpu_dc_detection
+ * (full_gpu/symwarpfastdeccuda.h:60-61).
+ */
+int fdb200_dc_detection(const int* knn_idx, const float* densities, int n, int k,
+                        const FdB200Opts* opts, int* parent_out, int* cores_out, int* num_cores_out);
+
+/*
+ * Labels: centers get 0..c-1; every other point takes the label of the first center on its
+ * parent chain, or 0 when the chain ends at a parent of -1. Replaces FastDECBase::final_cluster
+ * (fastdecbase.cpp:358-385) / gpu_final_cluster (full_gpu/symwarpfastdeccuda.h:70-72).
+ */
+int fdb200_final_cluster(const int* parent, int n, const int* centers, int c,
+                         const FdB200Opts* opts, int* labels_out);
+
+/*
+ * Multi-GPU building blocks (device pointers only). A shard computes the triangle tiles of its
+ * shard_rank / shard_count share into packed per-point partial lists; lists from all shards
+ * are then exchanged to their owners (by the caller's NCCL / torch.distributed) and merged.
+ * A packed entry is ((uint64)float_bits(d2) << 32) | index; lists are point-major, n * k,
+ * ascending, padded with UINT64_MAX. No counterpart in the reference (it is single-GPU); the
+ * merged result equals fdb200_knn's.
+ */
+int fdb200_knn_partial(const float* data_dev, int n, int d, int k, const FdB200Opts* opts,
+                       uint64_t* lists_dev, FdB200Stats* stats);
+
+/* lists_dev (n_points * k) <- k-smallest of itself and `nsrc` other list blocks of the same
+   points, stored one after another in srcs_dev (nsrc * n_points * k). */
+int fdb200_merge_lists(uint64_t* lists_dev, const uint64_t* srcs_dev, int nsrc, int n_points,
+                       int k, const FdB200Opts* opts);
+
+/* rank-major Euclidean distances / indices from packed point-major lists (device pointers). */
+int fdb200_lists_to_knn(const uint64_t* lists_dev, int n, int k, const FdB200Opts* opts,
+                        float* dist_dev, int* idx_dev);
+
+/*
+ * Fit from a finished kNN graph already on the device (rank-major dist / idx, k ranks): the
+ * stages after build_knn_graph (fastdecbase.cpp:173-227). data is the dim-major dataset
+ * (device pointer when opts->inputs_on_device).
+ */
+int fdb200_fit_from_knn(const float* data, const float* knn_dist_dev, const int* knn_idx_dev,
+                        int n, int d, int k, int c, const FdB200Opts* opts, int* centers_out,
+                        int* labels_out, float* densities_out, FdB200Stats* stats);
+
+/* Frees the library's cached device workspace on opts->device. */
+int fdb200_release(const FdB200Opts* opts);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FASTDEC_B200_H */

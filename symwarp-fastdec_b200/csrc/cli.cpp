@@ -1,0 +1,157 @@
+// cli.cpp -- command-line front end with the reference's config format and a `--backend b200`.
+//
+// Usage mirrors the reference CLI (test.cpp:185-357): [--gpu N] [--backend b200] [config_file],
+// config = 4 lines (CSV path, k, cluster count, run count; runs defaults to 1 when missing or
+// invalid, test.cpp:314-337). The CSV is read row-major and transposed to the dim-major layout
+// Fit takes (helper.cpp:9-63, test.cpp:110-115). Extra run-time switches replace the reference's
+// compile-time ones: --precision fp32|tf32 (USE_CUBLAS_TF32), --density laplacian|gaussian
+// (USE_GAUSSIAN_KERNEL), --engine auto|simt|tcgen05.
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "b200fastdec.h"
+
+static void usage(const char* prog)
+{
+    printf("Usage: %s [--gpu N] [--backend b200] [--precision fp32|tf32] [--density laplacian|gaussian]\n"
+           "          [--engine auto|simt|tcgen05] [config_file]\n", prog);
+    printf("  config_file    4 lines: dataset CSV, k, cluster count, run count (default ./config.txt)\n");
+}
+
+static bool read_csv(const std::string& path, std::vector<float>& rows, int& n, int& d)
+{
+    std::ifstream f(path);
+    if (!f) return false;
+    std::string line;
+    n = 0;
+    d = -1;
+    while (std::getline(f, line)) {
+        if (line.empty() || line == "\r") continue;
+        int cols = 0;
+        const char* p = line.c_str();
+        while (*p) {
+            char* end = nullptr;
+            const float v = strtof(p, &end);
+            if (end == p) break;
+            rows.push_back(v);
+            ++cols;
+            p = end;
+            while (*p == ',' || *p == ' ' || *p == '\r') ++p;
+        }
+        if (d < 0) d = cols;
+        if (cols != d) {
+            fprintf(stderr, "Error: row %d has %d columns, expected %d\n", n + 1, cols, d);
+            return false;
+        }
+        ++n;
+    }
+    return n > 0 && d > 0;
+}
+
+int main(int argc, char** argv)
+{
+    std::string cfg_path = "./config.txt";
+    FdB200Opts opts;
+    fdb200_opts_init(&opts);
+    int gpu = 0;
+    for (int i = 1; i < argc; ++i) {
+        const std::string a = argv[i];
+        auto value = [&](const char* flag) -> std::string {
+            if (i + 1 >= argc) {
+                printf("Error: %s requires a value\n", flag);
+                usage(argv[0]);
+                exit(EXIT_FAILURE);
+            }
+            return argv[++i];
+        };
+        if (a == "--gpu" || a == "-g") gpu = atoi(value("--gpu").c_str());
+        else if (a.rfind("--gpu=", 0) == 0) gpu = atoi(a.c_str() + 6);
+        else if (a == "--backend" || a == "-b" || a.rfind("--backend=", 0) == 0) {
+            const std::string b = (a.rfind("--backend=", 0) == 0) ? a.substr(10) : value("--backend");
+            if (b != "b200") {
+                printf("Error: invalid backend '%s'. This build provides 'b200'.\n", b.c_str());
+                return EXIT_FAILURE;
+            }
+        } else if (a == "--precision") {
+            const std::string v = value("--precision");
+            opts.precision = (v == "tf32") ? FDB200_TF32 : FDB200_FP32;
+        } else if (a == "--density") {
+            const std::string v = value("--density");
+            opts.density_kernel = (v == "gaussian") ? FDB200_GAUSSIAN : FDB200_LAPLACIAN;
+        } else if (a == "--engine") {
+            const std::string v = value("--engine");
+            opts.engine = (v == "simt") ? FDB200_ENGINE_SIMT : (v == "tcgen05") ? FDB200_ENGINE_TCGEN05
+                                                                              : FDB200_ENGINE_AUTO;
+        } else if (a == "--help" || a == "-h") {
+            usage(argv[0]);
+            return EXIT_SUCCESS;
+        } else {
+            cfg_path = a;
+        }
+    }
+
+    std::ifstream cf(cfg_path);
+    if (!cf) {
+        printf("Can't open the file: %s\n", cfg_path.c_str());
+        return EXIT_FAILURE;
+    }
+    std::vector<std::string> lines;
+    for (std::string l; std::getline(cf, l);) lines.push_back(l);
+    if (lines.size() < 3) {
+        printf("Error: the config needs at least 3 lines\n");
+        return EXIT_FAILURE;
+    }
+    const std::string data_file = lines[0];
+    const int k = atoi(lines[1].c_str());
+    const int c = atoi(lines[2].c_str());
+    int runs = 1;
+    if (lines.size() >= 4) {
+        runs = atoi(lines[3].c_str());
+        if (runs < 1) runs = 1;
+    }
+    printf("Read dataset from: %s\nNumber of nearest neighbors: %d\nNumber of clusters: %d\n"
+           "Number of runs: %d\nBackend: b200\n", data_file.c_str(), k, c, runs);
+
+    std::vector<float> rows;
+    int n = 0, d = 0;
+    if (!read_csv(data_file, rows, n, d)) {
+        printf("Error: could not read %s\n", data_file.c_str());
+        return EXIT_FAILURE;
+    }
+    if (n < k) {
+        printf("Error: k value is larger that the number of reference points\n");
+        return EXIT_FAILURE;
+    }
+    std::vector<float> dm((size_t)n * d);
+    for (int i = 0; i < n; ++i)
+        for (int t = 0; t < d; ++t) dm[(size_t)t * n + i] = rows[(size_t)i * d + t];
+
+    for (int run = 1; run <= runs; ++run) {
+        try {
+            B200FastDEC model(k, c, "b200_fastdec", gpu, &opts);
+            const auto t0 = std::chrono::steady_clock::now();
+            model.Fit(dm.data(), n, d);
+            const double wall =
+                std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+            const FdB200Stats& st = model.get_stats();
+            printf("Finished run %d of B200FastDEC: %.6f s (device: total %.3f ms, kNN %.3f ms, "
+                   "density+detection %.3f ms, DC reduction %.3f ms, labels %.3f ms; cores %d, k %d)\n",
+                   run, wall, st.total_ms, st.knn_ms, st.density_ms, st.dc_ms, st.labels_ms, st.num_cores,
+                   st.final_k);
+            printf("Cluster centers found: \nlength: %d\n[", (int)model.get_center_indices().size());
+            for (size_t i = 0; i < model.get_center_indices().size(); ++i)
+                printf("%s%d", i ? "," : "", model.get_center_indices()[i]);
+            printf("]\n\n");
+        } catch (const std::exception& e) {
+            fprintf(stderr, "%s\n", e.what());
+            return EXIT_FAILURE;
+        }
+    }
+    return EXIT_SUCCESS;
+}

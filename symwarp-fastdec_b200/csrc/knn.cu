@@ -1,0 +1,425 @@
+// knn.cu -- symmetric triangular exact self-kNN: round scheduler, SIMT distance tiles, per-point
+// list merge and the final rank-major ordering.
+//
+// Reference behaviour (cyberbull66/symwarp-fastdec): symtri_knn_cuda (symtriknncuda.cu:310-633)
+// walks the upper triangle of 9216^2 tiles one at a time, materialises each -2 X_r X_q^T tile in
+// HBM (cuBLAS SGEMM or the FDS FFMA tile, symtriknnfds.h:33-166) and feeds it to warp heaps with a
+// serial lane-0 insert (symtriknncuda.cu:104-210, symtriknnreverse.h:14-185). Its observable result
+// is, for every point, the lexicographic (d2, index) k-smallest of
+//     d2(i, j) = max((n_i + n_j) + (-2 * dot(x_i, x_j)), 0),   dot = fmaf chain over d = 0..D-1,
+// sorted ascending and sqrt'd (symtriknnsort.h:13-25, symtriknncuda.cu:225-234).
+//
+// B200 design (no tile in HBM, no serial heap):
+//   * The triangle is cut into 128-point blocks. Block pairs are visited by cyclic offset
+//     delta = (R - B) mod T, so every round touches every block the same number of times.
+//   * Each point keeps a sorted list of packed keys ((d2 bits << 32) | index) in HBM. A tile
+//     compares every pair against the row point's and the column point's list thresholds
+//     (snapshotted at round start) and appends survivors to per-point candidate buffers with one
+//     atomicAdd per (point, thread). A merge kernel then folds the candidates into the lists.
+//   * Rounds grow geometrically (each round adds about as many candidates per point as the list
+//     has seen before, scaled so that at most half the candidate buffer fills on average), so the
+//     stale-threshold cost stays O(k log N) candidates per point. A round whose buffers overflow is
+//     discarded and re-run in two halves, which always terminates (one offset never exceeds 256
+//     candidates per point and the buffer holds at least 256).
+//   * Because every pair is evaluated once and the lists keep the exact lexicographic k-smallest,
+//     the result equals the reference's FDS build bit for bit, ties included, whatever the order in
+//     which tiles run.
+#include "knn_common.cuh"
+
+#include <algorithm>
+#include <cfloat>
+#include <vector>
+
+namespace fdb {
+
+// ------------------------------------------------------------------ norms (symtriknncuda.cu:56-72)
+__global__ void norms_kernel(const float* __restrict__ x, int ldx, int n, int d, float* __restrict__ out)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float s = 0.0f;
+    for (int t = 0; t < d; ++t) {
+        const float v = x[(size_t)t * ldx + i];
+        s = __fmaf_rn(v, v, s);
+    }
+    out[i] = s;
+}
+
+void compute_norms(const float* x, int ldx, int n, int d, float* norms, cudaStream_t s)
+{
+    if (n <= 0) return;
+    norms_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, ldx, n, d, norms);
+    FDB_LAUNCHED();
+}
+
+constexpr int kSimtThreads = 256;
+constexpr int kDChunk = 32;
+
+// Exact FP32 tile: 128 x 128 pairs per CTA, 8 x 8 per thread, every dot product the sequential
+// fmaf chain over d = 0..D-1 (the FDS accumulation order, symtriknnfds.h:100-121).
+__global__ void __launch_bounds__(kSimtThreads) knn_tile_simt(TileRound r)
+{
+    __shared__ __align__(16) float As[kDChunk][kBlock];
+    __shared__ __align__(16) float Bs[kDChunk][kBlock];
+    int B, R;
+    if (!decode_unit(r, blockIdx.x, B, R)) return;
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int q0 = B * kBlock, r0 = R * kBlock;
+
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+
+    for (int d0 = 0; d0 < r.d; d0 += kDChunk) {
+        const int steps = min(kDChunk, r.d - d0);
+        for (int e = tid; e < kDChunk * kBlock; e += kSimtThreads) {
+            const int dd = e / kBlock, p = e % kBlock;
+            float va = 0.0f, vb = 0.0f;
+            if (dd < steps) {
+                const float* col = r.x + (size_t)(d0 + dd) * r.ldx;
+                if (q0 + p < r.n) va = col[q0 + p];
+                if (r0 + p < r.n) vb = col[r0 + p];
+            }
+            As[dd][p] = va;
+            Bs[dd][p] = vb;
+        }
+        __syncthreads();
+#pragma unroll 2
+        for (int dd = 0; dd < steps; ++dd) {
+            const float4 a0 = *reinterpret_cast<const float4*>(&As[dd][ty * 4]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&As[dd][64 + ty * 4]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&Bs[dd][tx * 4]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&Bs[dd][64 + tx * 4]);
+            const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+
+    // epilogue: exact d2, lexicographic admission against the snapshotted list thresholds
+    int gi[8], gj[8];
+    float nq[8], nr[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        gi[t] = q0 + ((t < 4) ? ty * 4 + t : 64 + ty * 4 + (t - 4));
+        gj[t] = r0 + ((t < 4) ? tx * 4 + t : 64 + tx * 4 + (t - 4));
+        nq[t] = (gi[t] < r.n) ? r.norms[gi[t]] : 0.0f;
+        nr[t] = (gj[t] < r.n) ? r.norms[gj[t]] : 0.0f;
+    }
+    uint64_t keys[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        if (gi[i] >= r.n) continue;
+        const uint64_t bound = r.thr[gi[i]];
+        int c = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (gj[j] >= r.n || gj[j] == gi[i]) continue;
+            const uint64_t key = pack_key(exact_d2(nq[i], nr[j], acc[i][j]), gj[j]);
+            if (key < bound) keys[c++] = key;
+        }
+        if (c) append_keys(r, gi[i], keys, c);
+    }
+    if (r.diag) return;   // diagonal units see both orders of every pair as rows
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        if (gj[j] >= r.n) continue;
+        const uint64_t bound = r.thr[gj[j]];
+        int c = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (gi[i] >= r.n) continue;
+            const uint64_t key = pack_key(exact_d2(nq[i], nr[j], acc[i][j]), gi[i]);
+            if (key < bound) keys[c++] = key;
+        }
+        if (c) append_keys(r, gj[j], keys, c);
+    }
+}
+
+// ------------------------------------------------------------------ merging
+__device__ __forceinline__ void warp_bitonic_sort(uint64_t* buf, int m, int lane)
+{
+    for (int size = 2; size <= m; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int t = lane; t < (m >> 1); t += 32) {
+                const int i = 2 * stride * (t / stride) + (t % stride);
+                const int j = i + stride;
+                const bool up = (i & size) == 0;
+                const uint64_t a = buf[i], b = buf[j];
+                if ((a > b) == up) {
+                    buf[i] = b;
+                    buf[j] = a;
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
+__host__ __device__ inline int next_pow2(int v)
+{
+    int m = 1;
+    while (m < v) m <<= 1;
+    return m;
+}
+
+// one warp per point: list <- k-smallest of (list, new candidates); threshold <- list[k-1]
+__global__ void knn_merge_kernel(uint64_t* __restrict__ lists, uint64_t* __restrict__ thr,
+                                 const uint64_t* __restrict__ cand, int* __restrict__ cnt, int n,
+                                 int k, int cap, int pw)
+{
+    extern __shared__ uint64_t msm[];
+    const int warps = blockDim.x >> 5, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int p = blockIdx.x * warps + w;
+    if (p >= n) return;
+    int c = cnt[p];
+    if (c == 0) return;
+    c = min(c, cap);
+    uint64_t* buf = msm + (size_t)w * pw;
+    const int tot = k + c, m = next_pow2(tot);
+    const uint64_t* lp = lists + (size_t)p * k;
+    const uint64_t* cp = cand + (size_t)p * cap;
+    for (int t = lane; t < m; t += 32)
+        buf[t] = (t < k) ? lp[t] : (t < tot ? cp[t - k] : kEmptyKey);
+    __syncwarp();
+    warp_bitonic_sort(buf, m, lane);
+    uint64_t* lo = lists + (size_t)p * k;
+    for (int t = lane; t < k; t += 32) lo[t] = buf[t];
+    if (lane == 0) {
+        thr[p] = buf[k - 1];
+        cnt[p] = 0;
+    }
+}
+
+// dst <- k-smallest of dst and nsrc other lists of the same points
+__global__ void merge_blocks_kernel(uint64_t* __restrict__ dst, const uint64_t* __restrict__ srcs,
+                                   int nsrc, int n, int k, int pw)
+{
+    extern __shared__ uint64_t msm[];
+    const int warps = blockDim.x >> 5, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int p = blockIdx.x * warps + w;
+    if (p >= n) return;
+    uint64_t* buf = msm + (size_t)w * pw;
+    const int tot = k * (nsrc + 1), m = next_pow2(tot);
+    for (int t = lane; t < m; t += 32) {
+        uint64_t v = kEmptyKey;
+        if (t < k) v = dst[(size_t)p * k + t];
+        else if (t < tot) {
+            const int b = t / k - 1, q = t % k;
+            v = srcs[((size_t)b * n + p) * k + q];
+        }
+        buf[t] = v;
+    }
+    __syncwarp();
+    warp_bitonic_sort(buf, m, lane);
+    for (int t = lane; t < k; t += 32) dst[(size_t)p * k + t] = buf[t];
+}
+
+static void merge_launch_shape(int pw, int* warps, size_t* smem)
+{
+    // keep at most 48 KB of dynamic shared memory per CTA unless one warp needs more
+    int w = (int)std::max<size_t>(1, std::min<size_t>(8, (48 * 1024) / ((size_t)pw * 8)));
+    *warps = w;
+    *smem = (size_t)w * pw * 8;
+}
+
+static void ensure_smem(const void* fn, size_t smem)
+{
+    if (smem > 48 * 1024)
+        FDB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+}
+
+void merge_list_blocks(Workspace&, uint64_t* dst, const uint64_t* srcs, int nsrc, int n, int k,
+                       cudaStream_t s)
+{
+    if (n <= 0 || k <= 0 || nsrc <= 0) return;
+    const int pw = next_pow2(k * (nsrc + 1));
+    FDB_REQUIRE((size_t)pw * 8 <= 200 * 1024, "merge of this many lists exceeds shared memory");
+    int warps;
+    size_t smem;
+    merge_launch_shape(pw, &warps, &smem);
+    ensure_smem((const void*)merge_blocks_kernel, smem);
+    merge_blocks_kernel<<<(n + warps - 1) / warps, warps * 32, smem, s>>>(dst, srcs, nsrc, n, k, pw);
+    FDB_LAUNCHED();
+}
+
+// ------------------------------------------------------------------ final ordering
+// symtriknncuda.cu:225-251: sqrtf(max(d2, 0)) and the rank-major transpose
+__global__ void lists_to_rank_major_kernel(const uint64_t* __restrict__ lists, int n, int k,
+                                           float* __restrict__ dist, int* __restrict__ idx)
+{
+    const int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= n) return;
+    const uint64_t* lp = lists + (size_t)p * k;
+    for (int q = 0; q < k; ++q) {
+        const uint64_t key = lp[q];
+        dist[(size_t)q * n + p] = sqrtf(fmaxf(__uint_as_float((uint32_t)(key >> 32)), 0.0f));
+        idx[(size_t)q * n + p] = (int)(uint32_t)key;
+    }
+}
+
+void lists_to_rank_major(const uint64_t* lists, int n, int k, float* dist, int* idx, cudaStream_t s)
+{
+    if (n <= 0 || k <= 0) return;
+    lists_to_rank_major_kernel<<<(n + 127) / 128, 128, 0, s>>>(lists, n, k, dist, idx);
+    FDB_LAUNCHED();
+}
+
+// ------------------------------------------------------------------ host scheduler
+static long long shard_pairs(int n, int T, int b_lo, int b_hi)
+{
+    auto bsz = [&](int b) -> long long { return std::min(kBlock, n - b * kBlock); };
+    const int dmax = T / 2;
+    long long tot = 0;
+    for (int b = b_lo; b < b_hi; ++b) {
+        const long long mb = bsz(b);
+        tot += mb * (mb - 1) / 2;
+        // valid offsets for this row block
+        int valid = dmax;
+        if ((T & 1) == 0 && dmax >= 1 && b >= T / 2) valid -= 1;
+        if (valid <= 0) continue;
+        if (b == T - 1) {
+            tot += mb * (long long)kBlock * valid;   // every partner of the last block is full
+            continue;
+        }
+        tot += mb * (long long)kBlock * valid;
+        // the one offset whose partner is the (possibly partial) last block
+        const int d0 = T - 1 - b;
+        const bool skipped = (T & 1) == 0 && d0 == T / 2 && b >= T / 2;
+        if (d0 >= 1 && d0 <= dmax && !skipped) tot += mb * (bsz(T - 1) - kBlock);
+    }
+    return tot;
+}
+
+static void launch_tile_round(const TileRound& r, int units, int engine, int precision, cudaStream_t s)
+{
+    if (engine == FDB200_ENGINE_TCGEN05) launch_tile_round_tc(r, units, precision, s);
+    else launch_tile_round_simt(r, units, s);
+}
+
+KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStream_t s)
+{
+    const int n = cfg.n, d = cfg.d, k = cfg.k;
+    FDB_REQUIRE(n >= 2 && d >= 1 && k >= 1 && k < n, "kNN needs n >= 2, d >= 1 and 1 <= k < n");
+    FDB_REQUIRE(cfg.shard_count >= 1 && cfg.shard_rank >= 0 && cfg.shard_rank < cfg.shard_count,
+                "bad shard_rank / shard_count");
+    KnnResult res;
+    const int T = (n + kBlock - 1) / kBlock;
+    const int b_lo = (int)((long long)T * cfg.shard_rank / cfg.shard_count);
+    const int b_hi = (int)((long long)T * (cfg.shard_rank + 1) / cfg.shard_count);
+    const int nb = b_hi - b_lo;
+    int cap = std::max(256, ((2 * k + 31) / 32) * 32);
+    if (cfg.cand_capacity > 0) cap = std::max(256, cfg.cand_capacity);
+    const int pw = next_pow2(k + cap);
+    FDB_REQUIRE((size_t)pw * 8 <= 200 * 1024, "k too large for the list merge (k + capacity > 25600)");
+
+    float* norms = ws.norms.as<float>(n);
+    uint64_t* lists = ws.lists.as<uint64_t>((size_t)n * k);
+    uint64_t* thr = ws.thr.as<uint64_t>(n);
+    uint64_t* cand = ws.cand.as<uint64_t>((size_t)n * cap);
+    int* cnt = ws.cnt.as<int>(n);
+    int* ovf = ws.flags.as<int>(16);
+    compute_norms(x, cfg.ldx, n, d, norms, s);
+    FDB_CUDA(cudaMemsetAsync(lists, 0xFF, sizeof(uint64_t) * (size_t)n * k, s));
+    FDB_CUDA(cudaMemsetAsync(thr, 0xFF, sizeof(uint64_t) * (size_t)n, s));
+    FDB_CUDA(cudaMemsetAsync(cnt, 0, sizeof(int) * (size_t)n, s));
+    FDB_CUDA(cudaMemsetAsync(ovf, 0, sizeof(int) * 16, s));
+    res.lists = lists;
+    res.pairs = shard_pairs(n, T, b_lo, b_hi);
+
+    int engine = cfg.engine;
+    if (engine == FDB200_ENGINE_AUTO) engine = tc_engine_supported(d) ? FDB200_ENGINE_TCGEN05 : FDB200_ENGINE_SIMT;
+    if (engine == FDB200_ENGINE_TCGEN05)
+        FDB_REQUIRE(tc_engine_supported(d), "the tcgen05 engine does not support this dimension/device");
+    FDB_REQUIRE(cfg.precision == FDB200_FP32 || engine == FDB200_ENGINE_TCGEN05,
+                "TF32 distances need the tcgen05 engine");
+    res.engine_used = engine;
+
+    int mwarps;
+    size_t msmem;
+    merge_launch_shape(pw, &mwarps, &msmem);
+    ensure_smem((const void*)knn_merge_kernel, msmem);
+
+    TileRound r{};
+    r.x = x; r.ldx = cfg.ldx; r.n = n; r.d = d; r.norms = norms; r.thr = thr; r.cand = cand;
+    r.cnt = cnt; r.cap = cap; r.ovf = ovf; r.T = T; r.b_lo = b_lo; r.nb = nb;
+
+    cudaEvent_t t0, t1;
+    FDB_CUDA(cudaEventCreate(&t0));
+    FDB_CUDA(cudaEventCreate(&t1));
+    const int dmax = T / 2;
+    bool diag_done = false;
+    int next_delta = 1;
+    double seen = kBlock - 1;   // candidates each point has been offered so far (approximate)
+    int pending = 0;            // block offsets in the round being retried, 0 = none
+    while (nb > 0 && (!diag_done || next_delta <= dmax)) {
+        int units, ndelta = 0;
+        if (!diag_done) {
+            r.diag = 1;
+            r.delta0 = 0;
+            units = nb;
+        } else {
+            if (pending > 0) {
+                ndelta = pending;
+            } else {
+                // expected admissions per point ~ new * k / seen; keep them near cap / 2
+                const double want = (double)cap * seen / (4.0 * kBlock * k);
+                ndelta = (int)std::max(1.0, std::min(want, (double)(dmax - next_delta + 1)));
+            }
+            r.diag = 0;
+            r.delta0 = next_delta;
+            units = nb * ndelta;
+        }
+        FDB_CUDA(cudaEventRecord(t0, s));
+        launch_tile_round(r, units, engine, cfg.precision, s);
+        FDB_CUDA(cudaEventRecord(t1, s));
+        FDB_CUDA(cudaMemcpyAsync(ws.pinned, ovf, sizeof(int), cudaMemcpyDeviceToHost, s));
+        FDB_CUDA(cudaStreamSynchronize(s));
+        float ms = 0.0f;
+        FDB_CUDA(cudaEventElapsedTime(&ms, t0, t1));
+        res.tile_ms += ms;
+        res.rounds++;
+        if (ws.pinned[0]) {
+            // discard the round: lists are untouched until the merge, so re-running is exact
+            res.overflow_reruns++;
+            FDB_CUDA(cudaMemsetAsync(cnt, 0, sizeof(int) * (size_t)n, s));
+            FDB_CUDA(cudaMemsetAsync(ovf, 0, sizeof(int), s));
+            if (r.diag || ndelta <= 1) {
+                cudaEventDestroy(t0);
+                cudaEventDestroy(t1);
+                throw Error(FDB200_EINTERNAL, "candidate buffer overflow on a single-offset round");
+            }
+            pending = ndelta / 2;
+            continue;
+        }
+        knn_merge_kernel<<<(n + mwarps - 1) / mwarps, mwarps * 32, msmem, s>>>(lists, thr, cand, cnt,
+                                                                               n, k, cap, pw);
+        FDB_LAUNCHED();
+        if (!diag_done) {
+            diag_done = true;
+        } else {
+            next_delta += ndelta;
+            seen += 2.0 * kBlock * ndelta;
+            pending = 0;
+        }
+    }
+    cudaEventDestroy(t0);
+    cudaEventDestroy(t1);
+    return res;
+}
+
+// SIMT engine launcher; the tcgen05 engine lives in knn_tc.cu
+void launch_tile_round_simt(const TileRound& r, int units, cudaStream_t s)
+{
+    if (units <= 0) return;
+    knn_tile_simt<<<units, kSimtThreads, 0, s>>>(r);
+    FDB_LAUNCHED();
+}
+
+}  // namespace fdb

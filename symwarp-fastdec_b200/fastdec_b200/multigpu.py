@@ -1,0 +1,91 @@
+"""Multi-GPU self-kNN: one process per GPU, the triangle sharded by row blocks.
+
+The reference is single-GPU (SURVEY: no NCCL/MPI anywhere). Here every rank evaluates the block
+pairs of its share of the triangle (fdb200_knn_partial with shard = (rank, world)) into partial
+lists for ALL points; a partial list is a lexicographic (d2, index) k-smallest of the candidates the
+rank saw, so the k-smallest of all ranks' partial lists is the exact answer (the selection is
+associative and commutative). Points are owned by contiguous ranges; one all-to-all moves every
+partial list to its owner, the owner merges the `world` copies on the GPU, and rank 0 gathers the
+merged ranges and runs the O(n k) tail (density, DC detection / reduction, labels) alone.
+
+The exchange (`exchange_to_owners`, `gather_to_root`) only uses torch.distributed collectives, so
+the same code runs over NCCL on B200s and over gloo on CPU tensors in the tests.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def owner_ranges(n: int, world: int):
+    """[start, stop) of the points owned by each rank (balanced contiguous ranges)."""
+    return [(n * r // world, n * (r + 1) // world) for r in range(world)]
+
+
+def exchange_to_owners(lists: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """lists: (n, k) int64 partial lists of all points on this rank. Returns (world, n_own, k):
+    block s is rank s's partial list for the points this rank owns."""
+    n, k = lists.shape
+    rng = owner_ranges(n, world)
+    n_own = rng[rank][1] - rng[rank][0]
+    out = torch.empty((world, n_own, k), dtype=lists.dtype, device=lists.device)
+    dist.all_to_all_single(out.view(-1), lists.reshape(-1),
+                           output_split_sizes=[n_own * k] * world,
+                           input_split_sizes=[(b - a) * k for a, b in rng])
+    return out
+
+
+def gather_to_root(merged: torch.Tensor, n: int, rank: int, world: int):
+    """merged: (n_own, k) final lists of this rank's points. Rank 0 receives the full (n, k)."""
+    k = merged.shape[1]
+    rng = owner_ranges(n, world)
+    if rank == 0:
+        full = torch.empty((n, k), dtype=merged.dtype, device=merged.device)
+        full[rng[0][0]:rng[0][1]].copy_(merged)
+        ops = [dist.P2POp(dist.irecv, full[a:b], s) for s, (a, b) in enumerate(rng) if s != 0 and b > a]
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+        return full
+    if merged.shape[0] > 0:
+        for req in dist.batch_isend_irecv([dist.P2POp(dist.isend, merged.contiguous(), 0)]):
+            req.wait()
+    return None
+
+
+class ShardedFit:
+    """One fit across `world` GPUs (see the module docstring). step() returns rank-local stats."""
+
+    def __init__(self, n, d, k, c, rank, world, device, stream_ptr, **opts):
+        import fastdec_b200 as fdb
+        self.fdb = fdb
+        self.n, self.d, self.k, self.c = n, d, k, c
+        self.rank, self.world, self.dev, self.sp = rank, world, device, stream_ptr
+        self.opts = opts
+        self.lists = torch.empty((n, k), dtype=torch.int64, device=device)
+        if rank == 0:
+            self.dist = torch.empty((k, n), dtype=torch.float32, device=device)
+            self.idx = torch.empty((k, n), dtype=torch.int32, device=device)
+
+    def step(self, x_dev, centers, labels):
+        fdb, n, k = self.fdb, self.n, self.k
+        st = fdb.knn_partial_device(x_dev, k, self.lists, (self.rank, self.world), stream=self.sp, **self.opts)
+        blocks = exchange_to_owners(self.lists, self.rank, self.world)
+        n_own = blocks.shape[1]
+        if n_own > 0:
+            fdb.merge_lists_device(blocks[0], blocks[1:], self.world - 1, n_own, k, stream=self.sp,
+                                   device=self.dev.index or 0)
+        full = gather_to_root(blocks[0], n, self.rank, self.world)
+        if self.rank == 0:
+            fdb.lists_to_knn_device(full, n, k, self.dist, self.idx, stream=self.sp, device=self.dev.index or 0)
+            tail = fdb.fit_from_knn_device(x_dev, self.dist, self.idx, k, self.c, centers, labels, stream=self.sp,
+                                           **{kk: v for kk, v in self.opts.items() if kk != "engine"})
+            for key in ("density_ms", "dc_ms", "labels_ms", "num_cores", "final_k"):
+                st[key] = tail[key]
+            st["launches"] = st.get("launches", 0) + tail.get("launches", 0) + 1   # + lists_to_knn
+        if n_own > 0:
+            st["launches"] = st.get("launches", 0) + 1                              # + merge
+        return st
+
+    def close(self):
+        self.lists = None
