@@ -134,17 +134,26 @@ __global__ void chunk_maps_kernel(const float* __restrict__ dist, int n, int k,
     m.par[0] = 0;
     m.par[1] = 1;
     const double start = pre[warp];
-    if (csum[warp] == 0.0) {
-        m.kind = 2;
-        m.e = 0;
-    } else if (!(start > 0.0)) {
+    const int p = warp * 32 + lane;
+    bool all_zero = true, bad = false;
+    if (p < n)
+        for (int q = 0; q < k; ++q) {
+            const float v = dist[(size_t)q * n + p];
+            all_zero &= (v == 0.0f);
+            bad |= !(v >= 0.0f);            // negative or NaN: only plain sequential addition is exact
+        }
+    all_zero = __all_sync(0xffffffffu, all_zero);
+    bad = __any_sync(0xffffffffu, bad);
+    if (bad || (!all_zero && !(start > 0.0))) {
         m.kind = 0;
+        m.e = 0;
+    } else if (all_zero) {
+        m.kind = 2;   // adding +0 never changes a non-negative sum
         m.e = 0;
     } else {
         const int e = ilogb(start);
         m.e = e;
         m.kind = 1;
-        const int p = warp * 32 + lane;
         if (p < n) {
             for (int q = 0; q < k; ++q) {
                 const double t = ldexp((double)dist[(size_t)q * n + p], 52 - e);  // v / u, exact
@@ -165,6 +174,7 @@ __global__ void chunk_maps_kernel(const float* __restrict__ dist, int n, int k,
                 }
             }
         }
+        if (__any_sync(0xffffffffu, m.kind == 0)) m.kind = 0;
     }
     m = warp_compose(m, lane);
     if (lane == 0) maps[warp] = m;
