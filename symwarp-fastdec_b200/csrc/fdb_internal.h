@@ -60,7 +60,7 @@ struct Workspace {
     cudaStream_t own_stream = nullptr;
     int* pinned = nullptr;                 // small pinned host scratch for flags / counters
     DevBuf data, norms, lists, thr, fthr, cand, cnt, flags;
-    DevBuf dist, idx, den, parent, cores, scan, mean_tmp, dc_tmp, labels_tmp, misc;
+    DevBuf dist, idx, den, parent, cores, scan, mean_tmp, dc_tmp, labels_tmp, misc, ops;
     void release_all();
 };
 
@@ -115,6 +115,9 @@ void compute_norms(const float* x, int ldx, int n, int d, float* norms, cudaStre
 
 // true when the tcgen05 tile engine can run this shape on the current device
 bool tc_engine_supported(int d);
+// builds the tcgen05 operands (point-major augmented rows) and their tensor maps
+void tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const float* norms, const float* U,
+                const uint64_t* thr, cudaStream_t s);
 
 // ---------------------------------------------------------------- density / detection
 // Sequential-order double mean of the first k ranks (rank stride n) -- bit-identical to the

@@ -57,7 +57,7 @@ constexpr int kDChunk = 32;
 
 // Exact FP32 tile: 128 x 128 pairs per CTA, 8 x 8 per thread, every dot product the sequential
 // fmaf chain over d = 0..D-1 (the FDS accumulation order, symtriknnfds.h:100-121).
-__global__ void __launch_bounds__(kSimtThreads) knn_tile_simt(TileRound r)
+__global__ void __launch_bounds__(kSimtThreads, 2) knn_tile_simt(TileRound r)
 {
     __shared__ __align__(16) float As[kDChunk][kBlock];
     __shared__ __align__(16) float Bs[kDChunk][kBlock];
@@ -112,33 +112,41 @@ __global__ void __launch_bounds__(kSimtThreads) knn_tile_simt(TileRound r)
         nq[t] = (gi[t] < r.n) ? r.norms[gi[t]] : 0.0f;
         nr[t] = (gj[t] < r.n) ? r.norms[gj[t]] : 0.0f;
     }
-    uint64_t keys[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         if (gi[i] >= r.n) continue;
         const uint64_t bound = r.thr[gi[i]];
-        int c = 0;
+        unsigned mask = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            if (gj[j] >= r.n || gj[j] == gi[i]) continue;
-            const uint64_t key = pack_key(exact_d2(nq[i], nr[j], acc[i][j]), gj[j]);
-            if (key < bound) keys[c++] = key;
+            const bool ok = gj[j] < r.n && gj[j] != gi[i] &&
+                            pack_key(exact_d2(nq[i], nr[j], acc[i][j]), gj[j]) < bound;
+            mask |= (ok ? 1u : 0u) << j;
         }
-        if (c) append_keys(r, gi[i], keys, c);
+        if (mask) {
+            int slot = atomicAdd(&r.cnt[gi[i]], __popc(mask));
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (mask & (1u << j)) append_at(r, gi[i], slot++, pack_key(exact_d2(nq[i], nr[j], acc[i][j]), gj[j]));
+        }
     }
     if (r.diag) return;   // diagonal units see both orders of every pair as rows
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         if (gj[j] >= r.n) continue;
         const uint64_t bound = r.thr[gj[j]];
-        int c = 0;
+        unsigned mask = 0;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            if (gi[i] >= r.n) continue;
-            const uint64_t key = pack_key(exact_d2(nq[i], nr[j], acc[i][j]), gi[i]);
-            if (key < bound) keys[c++] = key;
+            const bool ok = gi[i] < r.n && pack_key(exact_d2(nq[i], nr[j], acc[i][j]), gi[i]) < bound;
+            mask |= (ok ? 1u : 0u) << i;
         }
-        if (c) append_keys(r, gj[j], keys, c);
+        if (mask) {
+            int slot = atomicAdd(&r.cnt[gj[j]], __popc(mask));
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (mask & (1u << i)) append_at(r, gj[j], slot++, pack_key(exact_d2(nq[i], nr[j], acc[i][j]), gi[i]));
+        }
     }
 }
 
@@ -169,10 +177,13 @@ __host__ __device__ inline int next_pow2(int v)
     return m;
 }
 
-// one warp per point: list <- k-smallest of (list, new candidates); threshold <- list[k-1]
+// one warp per point: list <- k-smallest of (list, new candidates); threshold <- list[k-1];
+// filter bound U <- threshold plus the TF32 margin (filter_bound)
 __global__ void knn_merge_kernel(uint64_t* __restrict__ lists, uint64_t* __restrict__ thr,
+                                 float* __restrict__ U, const float* __restrict__ norms,
                                  const uint64_t* __restrict__ cand, int* __restrict__ cnt, int n,
-                                 int k, int cap, int pw)
+                                 int k, int cap, int pw, int d, int kp, int exact,
+                                 unsigned long long* __restrict__ admitted)
 {
     extern __shared__ uint64_t msm[];
     const int warps = blockDim.x >> 5, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -192,8 +203,28 @@ __global__ void knn_merge_kernel(uint64_t* __restrict__ lists, uint64_t* __restr
     uint64_t* lo = lists + (size_t)p * k;
     for (int t = lane; t < k; t += 32) lo[t] = buf[t];
     if (lane == 0) {
-        thr[p] = buf[k - 1];
+        const uint64_t t = buf[k - 1];
+        thr[p] = t;
         cnt[p] = 0;
+        const float T = (t == kEmptyKey) ? __int_as_float(0x7f800000) : __uint_as_float((uint32_t)(t >> 32));
+        U[p] = filter_bound(T, norms[p], d, kp, exact);
+        atomicAdd(admitted, (unsigned long long)c);
+    }
+}
+
+// per-point state before the first round: empty lists admit everything, padding nothing
+__global__ void init_point_state_kernel(int n, int rows, float* __restrict__ norms, uint64_t* __restrict__ thr,
+                                        float* __restrict__ U)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows) return;
+    if (i < n) {
+        thr[i] = kEmptyKey;
+        U[i] = __int_as_float(0x7f800000);
+    } else {
+        norms[i] = 0.0f;
+        thr[i] = 0;
+        U[i] = __int_as_float(0xff800000);
     }
 }
 
@@ -314,20 +345,27 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     const int b_lo = (int)((long long)T * cfg.shard_rank / cfg.shard_count);
     const int b_hi = (int)((long long)T * (cfg.shard_rank + 1) / cfg.shard_count);
     const int nb = b_hi - b_lo;
-    int cap = std::max(256, ((2 * k + 31) / 32) * 32);
+    // admissions per round have a fat right tail (the list's k-th key is itself a random order
+    // statistic), so rounds are sized for about a quarter of the buffer
+    int cap = std::max(512, ((4 * k + 31) / 32) * 32);
     if (cfg.cand_capacity > 0) cap = std::max(256, cfg.cand_capacity);
     const int pw = next_pow2(k + cap);
     FDB_REQUIRE((size_t)pw * 8 <= 200 * 1024, "k too large for the list merge (k + capacity > 25600)");
 
-    float* norms = ws.norms.as<float>(n);
+    // per-point arrays cover the padded last block and one poison block (tcgen05 tiles read them)
+    const int rows = T * kBlock + kBlock;
+    float* norms = ws.norms.as<float>(rows);
     uint64_t* lists = ws.lists.as<uint64_t>((size_t)n * k);
-    uint64_t* thr = ws.thr.as<uint64_t>(n);
+    uint64_t* thr = ws.thr.as<uint64_t>(rows);
+    float* U = ws.fthr.as<float>(rows);
     uint64_t* cand = ws.cand.as<uint64_t>((size_t)n * cap);
     int* cnt = ws.cnt.as<int>(n);
-    int* ovf = ws.flags.as<int>(16);
+    int* ovf = ws.flags.as<int>(16);   // [0] overflow, [1] tcgen05 error code, [2..3] admitted count
+    unsigned long long* admitted = reinterpret_cast<unsigned long long*>(ovf + 2);
     compute_norms(x, cfg.ldx, n, d, norms, s);
+    init_point_state_kernel<<<(rows + 255) / 256, 256, 0, s>>>(n, rows, norms, thr, U);
+    FDB_LAUNCHED();
     FDB_CUDA(cudaMemsetAsync(lists, 0xFF, sizeof(uint64_t) * (size_t)n * k, s));
-    FDB_CUDA(cudaMemsetAsync(thr, 0xFF, sizeof(uint64_t) * (size_t)n, s));
     FDB_CUDA(cudaMemsetAsync(cnt, 0, sizeof(int) * (size_t)n, s));
     FDB_CUDA(cudaMemsetAsync(ovf, 0, sizeof(int) * 16, s));
     res.lists = lists;
@@ -340,6 +378,9 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     FDB_REQUIRE(cfg.precision == FDB200_FP32 || engine == FDB200_ENGINE_TCGEN05,
                 "TF32 distances need the tcgen05 engine");
     res.engine_used = engine;
+    const int kp = ((d + 4 + 7) / 8) * 8;
+    const int exact = cfg.precision == FDB200_FP32 ? 1 : 0;
+    if (engine == FDB200_ENGINE_TCGEN05) tc_prepare(ws, x, cfg.ldx, n, d, norms, U, thr, s);
 
     int mwarps;
     size_t msmem;
@@ -347,7 +388,7 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     ensure_smem((const void*)knn_merge_kernel, msmem);
 
     TileRound r{};
-    r.x = x; r.ldx = cfg.ldx; r.n = n; r.d = d; r.norms = norms; r.thr = thr; r.cand = cand;
+    r.x = x; r.ldx = cfg.ldx; r.n = n; r.d = d; r.norms = norms; r.thr = thr; r.U = U; r.cand = cand;
     r.cnt = cnt; r.cap = cap; r.ovf = ovf; r.T = T; r.b_lo = b_lo; r.nb = nb;
 
     cudaEvent_t t0, t1;
@@ -363,28 +404,36 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
         if (!diag_done) {
             r.diag = 1;
             r.delta0 = 0;
+            r.ndelta = 0;
             units = nb;
         } else {
             if (pending > 0) {
                 ndelta = pending;
             } else {
-                // expected admissions per point ~ new * k / seen; keep them near cap / 2
-                const double want = (double)cap * seen / (4.0 * kBlock * k);
+                // expected admissions per point ~ new * k / seen; keep them near cap / 4
+                const double want = (double)cap * seen / (8.0 * kBlock * k);
                 ndelta = (int)std::max(1.0, std::min(want, (double)(dmax - next_delta + 1)));
             }
             r.diag = 0;
             r.delta0 = next_delta;
+            r.ndelta = ndelta;
             units = nb * ndelta;
         }
         FDB_CUDA(cudaEventRecord(t0, s));
         launch_tile_round(r, units, engine, cfg.precision, s);
         FDB_CUDA(cudaEventRecord(t1, s));
-        FDB_CUDA(cudaMemcpyAsync(ws.pinned, ovf, sizeof(int), cudaMemcpyDeviceToHost, s));
+        FDB_CUDA(cudaMemcpyAsync(ws.pinned, ovf, 2 * sizeof(int), cudaMemcpyDeviceToHost, s));
         FDB_CUDA(cudaStreamSynchronize(s));
         float ms = 0.0f;
         FDB_CUDA(cudaEventElapsedTime(&ms, t0, t1));
         res.tile_ms += ms;
         res.rounds++;
+        if (ws.pinned[1]) {
+            cudaEventDestroy(t0);
+            cudaEventDestroy(t1);
+            throw Error(FDB200_EINTERNAL, "tcgen05 tile kernel stopped on a bounded wait (code " +
+                                              std::to_string(ws.pinned[1]) + ")");
+        }
         if (ws.pinned[0]) {
             // discard the round: lists are untouched until the merge, so re-running is exact
             res.overflow_reruns++;
@@ -398,8 +447,8 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
             pending = ndelta / 2;
             continue;
         }
-        knn_merge_kernel<<<(n + mwarps - 1) / mwarps, mwarps * 32, msmem, s>>>(lists, thr, cand, cnt,
-                                                                               n, k, cap, pw);
+        knn_merge_kernel<<<(n + mwarps - 1) / mwarps, mwarps * 32, msmem, s>>>(
+            lists, thr, U, norms, cand, cnt, n, k, cap, pw, d, kp, exact, admitted);
         FDB_LAUNCHED();
         if (!diag_done) {
             diag_done = true;
@@ -411,6 +460,10 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     }
     cudaEventDestroy(t0);
     cudaEventDestroy(t1);
+    unsigned long long adm = 0;
+    FDB_CUDA(cudaMemcpyAsync(&adm, admitted, sizeof(adm), cudaMemcpyDeviceToHost, s));
+    FDB_CUDA(cudaStreamSynchronize(s));
+    res.candidates = (long long)adm;
     return res;
 }
 

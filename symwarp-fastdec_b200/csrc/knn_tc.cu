@@ -1,13 +1,681 @@
-// knn_tc.cu -- tcgen05 (5th-generation tensor core) distance-tile engine.
+// knn_tc.cu -- tcgen05 (5th-generation tensor core) distance-tile engine for sm_100a.
+//
+// What it computes is exactly what knn_tile_simt computes (the reference FDS build's d2 and the
+// lexicographic admission, see knn.cu); only the way candidates are found differs:
+//
+//   1. TF32 filter on the tensor cores. Each point is stored twice, point-major, with K = D + 4
+//      padded to a multiple of 8:
+//          A row i = [-2 x_i, 1, 1, nh_i, nl_i, 0...]      B row j = [x_j, nh_j, nl_j, 1, 1, 0...]
+//      where n = fmaf-chain |x|^2 (the reference's norm), nh = n with its low 13 mantissa bits
+//      cleared (exact in TF32) and nl = n - nh. One 128 x 256 x K TF32 MMA then gives
+//      acc(i, j) ~= n_i + n_j - 2 x_i.x_j = d2(i, j) straight in TMEM, without an epilogue FMA.
+//   2. Rigorous margin. |acc - d2_ref| <= c1 |x_i||x_j| + c2 (n_i + n_j) for every pair (TF32
+//      rounding of each coordinate <= 2^-10 relative, FP32 accumulation, the reference's own
+//      rounding). For a candidate that can enter point i's list (d2_ref <= T_i), |x_j| <=
+//      |x_i| + sqrt(T_i), so the per-point bound U_i = T_i + M_i(|x_i|, T_i) never rejects it.
+//      The merge kernel computes U after every round (fdb_margin below).
+//   3. Exact refine. A pair that passes acc <= U_row or acc <= U_col is recomputed with the
+//      sequential fmaf chain from the original FP32 coordinates, which sit in the same shared
+//      memory tiles (the B tile holds x, the A tile -2x, an exact scaling), and admitted with the
+//      exact lexicographic test. Precision TF32 skips the refine and keeps d2 = max(acc, 0).
+//
+// Kernel shape (persistent, one CTA per SM, 320 threads):
+//   warp 0      TMA producer: A tile (128 rows, resident for a work item) and double-buffered
+//               B tiles (two 128-point blocks = 256 rows), plus per-point bounds / norms /
+//               thresholds with bulk copies; K is split into 32-byte panels (SWIZZLE_32B, K-major)
+//   warp 1      TMEM owner and MMA issuer (one thread): K/8 tcgen05.mma kind::tf32 per tile into
+//               one of two 256-column TMEM accumulators, tcgen05.commit to an mbarrier
+//   warps 2..9  epilogue: tcgen05.ld 32 columns at a time, OR-accumulated two-sided filter,
+//               rare refine + append; release the accumulator and the B stage
+// Every mbarrier wait is bounded (about a second); on a timeout the CTA records an error code,
+// stops issuing work, frees its TMEM and returns, and the host reports the failure.
 #include "knn_common.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
 
 namespace fdb {
 
-bool tc_engine_supported(int) { return false; }
+namespace tc {
 
-void launch_tile_round_tc(const TileRound&, int, int, cudaStream_t)
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
+constexpr int kRows = 128;               // A rows per tile
+constexpr int kCols = 256;               // B rows per tile (two blocks)
+constexpr int kMaxKp = 72;               // K panels up to 9 (D <= 68)
+constexpr long long kWaitCycles = 2000000000ll;   // ~1 s at 2 GHz
+constexpr float kPoisonNorm = 1.2676506002282294e30f;   // 2^100, exact in TF32
+
+struct Args {
+    int n, d, kp, T, b_lo, nb, cap, exact;
+    int diag, delta0, ndelta, npairs, pairs_per_item, items;
+    int row_pad;                 // Npad: first poison row of the B array
+    const float* U;              // filter bounds (Npad + 128)
+    const float* nrm;            // exact fp32 norms (Npad + 128)
+    const uint64_t* thr;         // exact admission thresholds (Npad + 128)
+    uint64_t* cand;
+    int* cnt;
+    int* ovf;
+    int* err;
+};
+
+// ------------------------------------------------------------------ PTX wrappers
+__device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count)
 {
-    throw Error(FDB200_EINVAL, "the tcgen05 engine is not available in this build");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// bounded wait: false on timeout or when another role aborted the CTA
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err,
+                                          int code)
+{
+    const long long t0 = clock64();
+    while (!mbar_try_wait(b, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > kWaitCycles) {
+            *abort_flag = 1;
+            atomicCAS(err, 0, code);
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            su32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(su32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     su32(dst)),
+                 "l"(src), "r"(bytes), "r"(su32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major, SWIZZLE_32B panel: rows 32 B apart, 8-row groups 256 B apart
+__device__ __forceinline__ uint64_t sw32_desc(uint32_t saddr)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)1 << 16;            // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(256 >> 4) << 32;   // stride byte offset: 8 rows x 32 B
+    d |= (uint64_t)1 << 46;            // descriptor version for sm_100
+    d |= (uint64_t)6 << 61;            // SWIZZLE_32B
+    return d;
+}
+
+// kind::tf32, D = F32, A = B = TF32, both K-major, M = 128, N = 256
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kCols >> 3) << 17) |
+                            ((uint32_t)(kRows >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accum)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accum)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
+{
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int t = 0; t < 32; ++t) v[t] = __uint_as_float(r[t]);
+}
+
+// ------------------------------------------------------------------ shared memory plan
+struct Smem {
+    // offsets in bytes from the 1024-aligned base
+    uint32_t a, b0, b1, arow_u, arow_n, arow_t, bcol_u[2], bcol_n[2], bcol_t[2], scratch, bars, misc, total;
+};
+
+__host__ __device__ inline Smem smem_plan(int kp)
+{
+    Smem s;
+    const uint32_t panels = (uint32_t)kp / 8;
+    uint32_t o = 0;
+    s.a = o;
+    o += panels * kRows * 32;
+    s.b0 = o;
+    o += panels * kCols * 32;
+    s.b1 = o;
+    o += panels * kCols * 32;
+    s.arow_u = o;
+    o += kRows * 4;
+    s.arow_n = o;
+    o += kRows * 4;
+    s.arow_t = o;
+    o += kRows * 8;
+    for (int q = 0; q < 2; ++q) {
+        s.bcol_u[q] = o;
+        o += kCols * 4;
+        s.bcol_n[q] = o;
+        o += kCols * 4;
+        s.bcol_t[q] = o;
+        o += kCols * 8;
+    }
+    s.scratch = o;
+    o += kEpiWarps * 32 * 33 * 4;
+    o = (o + 15) & ~15u;
+    s.bars = o;
+    o += 16 * 8;
+    s.misc = o;
+    o += 64;
+    s.total = o;
+    return s;
+}
+
+// element (row, k) of a K-major SW32 panel set: panel k/8, 16-byte chunk swizzled by row bit 2
+__device__ __forceinline__ const float4* panel_chunk(const unsigned char* base, int rows_per_panel, int row,
+                                                     int chunk)
+{
+    const int panel = chunk >> 1, half = chunk & 1;
+    const int phys = half ^ ((row >> 2) & 1);
+    return reinterpret_cast<const float4*>(base + (size_t)panel * rows_per_panel * 32 + row * 32 + phys * 16);
+}
+
+// exact d2 of (A row ra, B row rb) from the tiles: fmaf chain over d = 0..D-1
+__device__ __forceinline__ float refine_d2(const unsigned char* abase, int ra, const unsigned char* bbase, int rb,
+                                           int d, float na, float nb)
+{
+    float dot = 0.0f;
+    const int chunks = (d + 3) >> 2;
+    for (int c = 0; c < chunks; ++c) {
+        const float4 av = *panel_chunk(abase, kRows, ra, c);
+        const float4 bv = *panel_chunk(bbase, kCols, rb, c);
+        const float a4[4] = {av.x, av.y, av.z, av.w};
+        const float b4[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            if (c * 4 + e < d) dot = __fmaf_rn(__fmul_rn(-0.5f, a4[e]), b4[e], dot);
+    }
+    return exact_d2(na, nb, dot);
+}
+
+// unit (item, index inside item) -> Q block and the two R blocks (-1 = poison half)
+struct Unit {
+    int B, R0, R1;
+};
+
+__device__ __forceinline__ int item_units(const Args& a, int item, int& p_lo)
+{
+    if (a.diag) {
+        p_lo = 0;
+        return 1;
+    }
+    const int chunk = item / a.nb;
+    p_lo = chunk * a.pairs_per_item;
+    return min(a.npairs, p_lo + a.pairs_per_item) - p_lo;
+}
+
+__device__ __forceinline__ Unit make_unit(const Args& a, int item, int p)
+{
+    Unit u;
+    u.B = a.b_lo + item % a.nb;
+    if (a.diag) {
+        u.R0 = u.B;
+        u.R1 = -1;
+        return u;
+    }
+    int Rs[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int off = 2 * p + h;
+        const int dl = a.delta0 + off;
+        int R = -1;
+        if (off < a.ndelta && !((a.T & 1) == 0 && dl == a.T / 2 && u.B >= a.T / 2)) {
+            R = u.B + dl;
+            if (R >= a.T) R -= a.T;
+        }
+        Rs[h] = R;
+    }
+    u.R0 = Rs[0];
+    u.R1 = Rs[1];
+    return u;
+}
+
+__device__ __forceinline__ void tc_append(const Args& a, int p, uint64_t key)
+{
+    const int slot = atomicAdd(&a.cnt[p], 1);
+    if (slot < a.cap) a.cand[(size_t)p * a.cap + slot] = key;
+    else atomicOr(a.ovf, 1);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    knn_tile_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, Args a)
+{
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* sm = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const Smem P = smem_plan(a.kp);
+    const int panels = a.kp / 8;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P.bars);
+    uint64_t* a_full = bars + 0;
+    uint64_t* a_empty = bars + 1;
+    uint64_t* b_full = bars + 2;      // [2]
+    uint64_t* b_empty = bars + 4;     // [2]
+    uint64_t* acc_full = bars + 6;    // [2]
+    uint64_t* acc_empty = bars + 8;   // [2]
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + P.misc);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + P.misc + 16);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        mbar_init(a_full, 1);
+        mbar_init(a_empty, kEpiWarps);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], kEpiWarps);
+            mbar_init(&acc_full[s], 1);
+            mbar_init(&acc_empty[s], kEpiWarps);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const uint32_t a_bytes = (uint32_t)panels * kRows * 32;
+    const uint32_t b_half_bytes = (uint32_t)panels * kRows * 32;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            int g = 0;
+            bool ok = true;
+            for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
+                if (!mbar_wait(a_empty, (t & 1) ^ 1, abort_flag, a.err, 1)) { ok = false; break; }
+                const int B = a.b_lo + item % a.nb;
+                mbar_expect_tx(a_full, a_bytes + kRows * 16);
+                for (int p = 0; p < panels; ++p)
+                    tma_load_2d(sm + P.a + p * kRows * 32, &mapA, p * 8, B * kRows, a_full);
+                bulk_load(sm + P.arow_u, a.U + (size_t)B * kRows, kRows * 4, a_full);
+                bulk_load(sm + P.arow_n, a.nrm + (size_t)B * kRows, kRows * 4, a_full);
+                bulk_load(sm + P.arow_t, a.thr + (size_t)B * kRows, kRows * 8, a_full);
+                int p_lo;
+                const int nu = item_units(a, item, p_lo);
+                for (int uix = 0; uix < nu; ++uix, ++g) {
+                    const int s = g & 1;
+                    if (!mbar_wait(&b_empty[s], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 2)) { ok = false; break; }
+                    const Unit u = make_unit(a, item, p_lo + uix);
+                    unsigned char* bb = sm + (s ? P.b1 : P.b0);
+                    mbar_expect_tx(&b_full[s], 2 * b_half_bytes + 2 * kRows * 16);
+                    const int rows0 = (u.R0 >= 0 ? u.R0 * kRows : a.row_pad);
+                    const int rows1 = (u.R1 >= 0 ? u.R1 * kRows : a.row_pad);
+                    for (int p = 0; p < panels; ++p) {
+                        tma_load_2d(bb + p * kCols * 32, &mapB, p * 8, rows0, &b_full[s]);
+                        tma_load_2d(bb + p * kCols * 32 + kRows * 32, &mapB, p * 8, rows1, &b_full[s]);
+                    }
+                    bulk_load(sm + P.bcol_u[s], a.U + rows0, kRows * 4, &b_full[s]);
+                    bulk_load(sm + P.bcol_u[s] + kRows * 4, a.U + rows1, kRows * 4, &b_full[s]);
+                    bulk_load(sm + P.bcol_n[s], a.nrm + rows0, kRows * 4, &b_full[s]);
+                    bulk_load(sm + P.bcol_n[s] + kRows * 4, a.nrm + rows1, kRows * 4, &b_full[s]);
+                    bulk_load(sm + P.bcol_t[s], a.thr + rows0, kRows * 8, &b_full[s]);
+                    bulk_load(sm + P.bcol_t[s] + kRows * 8, a.thr + rows1, kRows * 8, &b_full[s]);
+                }
+            }
+            // on abort, let copies already issued land before the CTA exits (bounded)
+            if (!ok) {
+                const long long t0 = clock64();
+                for (int q = 0; q < 2 && q < g; ++q) {
+                    const int gl = g - 1 - q;
+                    while (!mbar_try_wait(&b_full[gl & 1], (gl >> 1) & 1) && clock64() - t0 < kWaitCycles) {
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            int g = 0;
+            bool ok = true;
+            for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
+                if (!mbar_wait(a_full, t & 1, abort_flag, a.err, 3)) { ok = false; break; }
+                int p_lo;
+                const int nu = item_units(a, item, p_lo);
+                for (int uix = 0; uix < nu; ++uix, ++g) {
+                    const int s = g & 1;
+                    if (!mbar_wait(&b_full[s], (g >> 1) & 1, abort_flag, a.err, 4)) { ok = false; break; }
+                    if (!mbar_wait(&acc_empty[s], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 5)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + (uint32_t)(s * kCols);
+                    const uint32_t abase = su32(sm + P.a), bbase = su32(sm + (s ? P.b1 : P.b0));
+                    for (int p = 0; p < panels; ++p)
+                        mma_tf32(d_tmem, sw32_desc(abase + p * kRows * 32), sw32_desc(bbase + p * kCols * 32),
+                                 p > 0 ? 1u : 0u);
+                    mma_commit(&acc_full[s]);
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        const int e = warp - 2;                 // 0..7
+        const int quad = warp & 3;              // TMEM lanes this warp may read
+        const int half = e >> 2;                // column half of the tile
+        const int ra = quad * 32 + lane;        // this thread's A row (tile-local)
+        float* scr = reinterpret_cast<float*>(sm + P.scratch) + (size_t)e * 32 * 33;
+        int g = 0;
+        bool ok = true;
+        for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
+            if (!mbar_wait(a_full, t & 1, abort_flag, a.err, 6)) { ok = false; break; }
+            const float* au = reinterpret_cast<const float*>(sm + P.arow_u);
+            const float Ui = au[ra];
+            const float ni = reinterpret_cast<const float*>(sm + P.arow_n)[ra];
+            const uint64_t ti = reinterpret_cast<const uint64_t*>(sm + P.arow_t)[ra];
+            int p_lo;
+            const int nu = item_units(a, item, p_lo);
+            for (int uix = 0; uix < nu; ++uix, ++g) {
+                const int s = g & 1;
+                if (!mbar_wait(&acc_full[s], (g >> 1) & 1, abort_flag, a.err, 7)) { ok = false; break; }
+                tc_fence_after();
+                const Unit u = make_unit(a, item, p_lo + uix);
+                const int gi = u.B * kRows + ra;
+                const unsigned char* bb = sm + (s ? P.b1 : P.b0);
+                const float* cu = reinterpret_cast<const float*>(sm + P.bcol_u[s]);
+                const float* cn = reinterpret_cast<const float*>(sm + P.bcol_n[s]);
+                const uint64_t* ct = reinterpret_cast<const uint64_t*>(sm + P.bcol_t[s]);
+                const int rblk = half ? u.R1 : u.R0;
+                for (int c = 0; c < 4 && rblk >= 0; ++c) {
+                    const int cb = half * 128 + c * 32;
+                    float v[32];
+                    tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(s * kCols + cb), v);
+                    bool any = false;
+#pragma unroll
+                    for (int q = 0; q < 32; q += 4) {
+                        const float4 u4 = *reinterpret_cast<const float4*>(cu + cb + q);
+                        any |= (v[q] <= Ui) | (v[q] <= u4.x);
+                        any |= (v[q + 1] <= Ui) | (v[q + 1] <= u4.y);
+                        any |= (v[q + 2] <= Ui) | (v[q + 2] <= u4.z);
+                        any |= (v[q + 3] <= Ui) | (v[q + 3] <= u4.w);
+                    }
+                    if (!__any_sync(0xffffffffu, any)) continue;
+                    // slow path: stash the row so survivors can be visited with a dynamic index
+#pragma unroll
+                    for (int q = 0; q < 32; ++q) scr[lane * 33 + q] = v[q];
+                    __syncwarp();
+                    if (any && gi < a.n) {
+                        for (int q = 0; q < 32; ++q) {
+                            const float acc = scr[lane * 33 + q];
+                            const float Uj = cu[cb + q];
+                            const bool row_ok = acc <= Ui;
+                            const bool col_ok = !a.diag && acc <= Uj;
+                            if (!row_ok && !col_ok) continue;
+                            const int jloc = cb + q;
+                            const int gj = rblk * kRows + c * 32 + q;
+                            if (gj == gi || gj >= a.n) continue;   // self pair / padding
+                            const float nj = cn[jloc];
+                            const float d2 = a.exact ? refine_d2(sm + P.a, ra, bb, jloc, a.d, ni, nj)
+                                                     : fmaxf(acc, 0.0f);
+                            if (row_ok) {
+                                const uint64_t key = pack_key(d2, gj);
+                                if (key < ti) tc_append(a, gi, key);
+                            }
+                            if (col_ok) {
+                                const uint64_t key = pack_key(d2, gi);
+                                if (key < ct[jloc]) tc_append(a, gj, key);
+                            }
+                        }
+                    }
+                    __syncwarp();
+                }
+                tc_fence_before();
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&acc_empty[s]);
+                    mbar_arrive(&b_empty[s]);
+                }
+            }
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(a_empty);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512) : "memory");
+}
+
+// ------------------------------------------------------------------ data preparation
+// A / B rows (point-major, kp floats) from the dim-major dataset; padded rows are poison.
+__global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, int d, int kp, int rows_a,
+                                  int rows_b, const float* __restrict__ norms, float* __restrict__ A,
+                                  float* __restrict__ Bm)
+{
+    const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t total = (size_t)rows_b * kp;
+    if (t >= total) return;
+    const int i = (int)(t / kp), k = (int)(t % kp);
+    float va = 0.0f, vb = 0.0f;
+    if (i < n) {
+        const float nn = norms[i];
+        const float nh = __uint_as_float(__float_as_uint(nn) & 0xFFFFE000u);
+        const float nl = __fsub_rn(nn, nh);
+        if (k < d) {
+            const float xv = x[(size_t)k * ldx + i];
+            va = __fmul_rn(-2.0f, xv);
+            vb = xv;
+        } else if (k == d) {
+            va = 1.0f;
+            vb = nh;
+        } else if (k == d + 1) {
+            va = 1.0f;
+            vb = nl;
+        } else if (k == d + 2) {
+            va = nh;
+            vb = 1.0f;
+        } else if (k == d + 3) {
+            va = nl;
+            vb = 1.0f;
+        }
+    } else {
+        // padding / poison row: its product with any real row is 2^100, above every finite bound
+        if (k == d + 2) va = kPoisonNorm;
+        if (k == d) vb = kPoisonNorm;
+    }
+    if (i < rows_a) A[t] = va;
+    Bm[t] = vb;
+}
+
+}  // namespace tc
+
+// ------------------------------------------------------------------ host side
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        FDB_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !p) throw Error(FDB200_ECUDA, "cuTensorMapEncodeTiled unavailable");
+        fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    }
+    return fn;
+}
+
+void make_map(CUtensorMap* m, const float* base, int rows, int kp)
+{
+    const cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)kp * 4};
+    const cuuint32_t box[2] = {8, (cuuint32_t)tc::kRows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw Error(FDB200_ECUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+}
+
+struct TcState {
+    int device = -1, n = 0, d = 0, kp = 0, npad = 0;
+    const float* x = nullptr;
+    float *A = nullptr, *B = nullptr, *U = nullptr, *nrm = nullptr;   // U/nrm/thr: scheduler-owned
+    uint64_t* thr = nullptr;
+    CUtensorMap mapA, mapB;
+    int sms = 0;
+};
+
+TcState g_state;   // the prepared operands of the current kNN call (one per process)
+
+}  // namespace
+
+bool tc_engine_supported(int d)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, dev) != cudaSuccess) return false;
+    const int kp = ((d + 4 + 7) / 8) * 8;
+    return p.major == 10 && p.minor == 0 && kp <= tc::kMaxKp && tc::smem_plan(kp).total + 1024 <= 227 * 1024;
+}
+
+// Prepares the TF32 operand rows and tensor maps for one kNN call; the per-point bounds,
+// norms and thresholds (rows_b entries each) belong to the scheduler.
+void tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const float* norms, const float* U,
+                const uint64_t* thr, cudaStream_t s)
+{
+    TcState& st = g_state;
+    const int kp = ((d + 4 + 7) / 8) * 8;
+    const int T = (n + kBlock - 1) / kBlock;
+    const int npad = T * kBlock;
+    const int rows_b = npad + kBlock;     // + one poison block
+    const size_t a_bytes = sizeof(float) * (size_t)npad * kp;
+    const size_t b_bytes = sizeof(float) * (size_t)rows_b * kp;
+    char* mem = (char*)ws.ops.ensure(a_bytes + b_bytes + 2048);
+    auto align = [](char* p) { return (char*)(((uintptr_t)p + 1023) & ~(uintptr_t)1023); };
+    st.A = (float*)align(mem);
+    st.B = (float*)align((char*)st.A + a_bytes);
+    const size_t total = (size_t)rows_b * kp;
+    tc::build_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(x, ldx, n, d, kp, npad, rows_b, norms,
+                                                                          st.A, st.B);
+    FDB_LAUNCHED();
+    make_map(&st.mapA, st.A, npad, kp);
+    make_map(&st.mapB, st.B, rows_b, kp);
+    int dev = 0;
+    FDB_CUDA(cudaGetDevice(&dev));
+    FDB_CUDA(cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev));
+    st.device = dev;
+    st.n = n;
+    st.d = d;
+    st.kp = kp;
+    st.npad = npad;
+    st.x = x;
+    st.U = const_cast<float*>(U);
+    st.nrm = const_cast<float*>(norms);
+    st.thr = const_cast<uint64_t*>(thr);
+}
+
+void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStream_t s)
+{
+    (void)units;
+    TcState& st = g_state;
+    tc::Args a{};
+    a.n = r.n;
+    a.d = r.d;
+    a.kp = st.kp;
+    a.T = r.T;
+    a.b_lo = r.b_lo;
+    a.nb = r.nb;
+    a.cap = r.cap;
+    a.exact = precision == FDB200_FP32 ? 1 : 0;
+    a.diag = r.diag;
+    a.delta0 = r.delta0;
+    a.ndelta = r.ndelta;
+    a.row_pad = st.npad;
+    a.U = st.U;
+    a.nrm = st.nrm;
+    a.thr = st.thr;
+    a.cand = r.cand;
+    a.cnt = r.cnt;
+    a.ovf = r.ovf;
+    a.err = r.ovf + 1;
+    if (r.diag) {
+        a.npairs = 1;
+        a.pairs_per_item = 1;
+        a.items = r.nb;
+    } else {
+        a.npairs = (r.ndelta + 1) / 2;
+        // about 8 items per CTA so the tail of a round stays short
+        const long long want_items = 8ll * st.sms;
+        int ppi = (int)std::max<long long>(1, ((long long)a.npairs * r.nb + want_items - 1) / want_items);
+        ppi = std::min(ppi, a.npairs);
+        a.pairs_per_item = ppi;
+        a.items = r.nb * ((a.npairs + ppi - 1) / ppi);
+    }
+    if (a.items <= 0) return;
+    const tc::Smem P = tc::smem_plan(st.kp);
+    const size_t smem = P.total + 1024;
+    static bool attr_set = false;
+    if (!attr_set) {
+        FDB_CUDA(cudaFuncSetAttribute(tc::knn_tile_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        attr_set = true;
+    }
+    const int grid = std::min(a.items, st.sms);
+    tc::knn_tile_tc<<<grid, tc::kThreads, smem, s>>>(st.mapA, st.mapB, a);
+    FDB_LAUNCHED();
 }
 
 }  // namespace fdb

@@ -10,6 +10,9 @@ import fastdec_b200.datasets as ds
 pytestmark = pytest.mark.gpu
 
 
+ENGINES = ["simt", "tcgen05"]
+
+
 def _check_equal(fdb, oracle, x, k, **kw):
     dist, idx, st = fdb.knn(x, k, **kw)
     od, oi = oracle.knn(x, k)
@@ -26,17 +29,19 @@ def test_spiral_knn_bit_exact(fdb, oracle, spiral_dm):
     (2, 1, 1), (3, 2, 2), (33, 3, 8), (129, 1, 5), (257, 8, 64), (1000, 33, 20),
     (1000, 50, 45), (3001, 16, 20), (640, 100, 10), (5000, 2, 7), (300, 64, 299),
 ])
-def test_random_shapes_bit_exact(fdb, oracle, n, d, k):
+@pytest.mark.parametrize("engine", ENGINES)
+def test_random_shapes_bit_exact(fdb, oracle, n, d, k, engine):
     rng = np.random.default_rng(n * 131 + d)
     x = rng.uniform(-1, 1, (d, n)).astype(np.float32)
-    _check_equal(fdb, oracle, x, k)
+    _check_equal(fdb, oracle, x, k, engine=engine if d <= 68 else "simt")
 
 
 @pytest.mark.parametrize("k", [1, 8, 64, 200])
-def test_integer_grid_ties_bit_exact(fdb, oracle, k):
+@pytest.mark.parametrize("engine", ENGINES)
+def test_integer_grid_ties_bit_exact(fdb, oracle, k, engine):
     # small-integer coordinates: many exact ties and duplicate points (zero distances)
     x = ds.small_integer_grid(1500, 4, levels=5, seed=k)
-    _check_equal(fdb, oracle, x, k)
+    _check_equal(fdb, oracle, x, k, engine=engine)
 
 
 def test_gmm_20k_bit_exact(fdb, oracle):
@@ -52,7 +57,7 @@ def test_glove_like_sample_bit_exact(fdb, oracle):
 
 def test_small_capacity_forces_overflow_reruns_and_stays_exact(fdb, oracle):
     x = ds.small_integer_grid(3000, 3, levels=4, seed=5)   # heavy ties keep many candidates alive
-    st = _check_equal(fdb, oracle, x, 150, cand_capacity=256)
+    st = _check_equal(fdb, oracle, x, 150, cand_capacity=256, engine="simt")
     assert st["rounds"] >= 2
 
 
@@ -65,12 +70,13 @@ def test_knn_argument_errors(fdb):
     assert d.shape == (3, 1)
 
 
-def test_large_properties_and_sampled_rows(fdb, oracle):
+@pytest.mark.parametrize("engine", ["simt", "tcgen05"])
+def test_large_properties_and_sampled_rows(fdb, oracle, engine):
     """200k x 50 (larger than L2): sorted lists, no self, distinct neighbours, and exact
     agreement with the oracle on sampled rows."""
     n, k = 200_000, 45
     x = ds.embedding_cloud(n=n, d=50, seed=23)
-    dist, idx, st = fdb.knn(x, k)
+    dist, idx, st = fdb.knn(x, k, engine=engine)
     assert st["pairs"] == n * (n - 1) // 2
     assert (idx != np.arange(n)[None, :]).all()
     assert (np.diff(dist, axis=0) >= 0).all()

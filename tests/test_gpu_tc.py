@@ -1,0 +1,67 @@
+"""tcgen05 engine: bit-exact FP32 parity with the oracle (TF32 filter + exact refine), and the
+TF32 distance mode against exact distances within TF32 error."""
+import numpy as np
+import pytest
+
+import fastdec_b200.datasets as ds
+
+pytestmark = pytest.mark.gpu
+
+
+def _exact(fdb, oracle, x, k, **kw):
+    dist, idx, st = fdb.knn(x, k, engine="tcgen05", **kw)
+    assert st["engine_used"] == 2
+    od, oi = oracle.knn(x, k)
+    assert np.array_equal(idx, oi), f"first index mismatch at {np.argwhere(idx != oi)[:3].tolist()}"
+    assert np.array_equal(dist.view(np.uint32), od.view(np.uint32))
+    return st
+
+
+@pytest.mark.parametrize("n,d,k", [(2, 1, 1), (129, 3, 5), (300, 2, 7), (1000, 16, 20), (2049, 50, 45),
+                                   (5000, 8, 31), (3000, 64, 10), (777, 68, 30)])
+def test_tc_bit_exact_small(fdb, oracle, n, d, k):
+    rng = np.random.default_rng(7 * n + d)
+    x = rng.uniform(-1, 1, (d, n)).astype(np.float32)
+    _exact(fdb, oracle, x, k)
+
+
+def test_tc_spiral(fdb, oracle, spiral_dm):
+    _exact(fdb, oracle, spiral_dm, 7)
+
+
+def test_tc_ties_and_duplicates(fdb, oracle):
+    _exact(fdb, oracle, ds.small_integer_grid(2500, 5, levels=4, seed=2), 60)
+
+
+def test_tc_offset_data_large_norms(fdb, oracle):
+    # far from the origin: large |x| stresses the dot-product form of the TF32 margin
+    x = ds.gmm_isotropic(n=6000, d=16, seed=5) + 40.0
+    _exact(fdb, oracle, x.astype(np.float32), 20)
+
+
+def test_tc_glove_like(fdb, oracle):
+    _exact(fdb, oracle, ds.embedding_cloud(n=30000, d=50, seed=8), 45)
+
+
+def test_tc_matches_simt_on_large_input(fdb):
+    x = ds.embedding_cloud(n=150_000, d=50, seed=9)
+    a = fdb.knn(x, 45, engine="tcgen05")
+    b = fdb.knn(x, 45, engine="simt")
+    assert np.array_equal(a[1], b[1]) and np.array_equal(a[0], b[0])
+    assert a[2]["pairs"] == b[2]["pairs"]
+
+
+def test_tf32_mode_distances_close(fdb, oracle):
+    x = ds.gmm_isotropic(n=8000, d=16, seed=3)
+    dist, idx, st = fdb.knn(x, 20, engine="tcgen05", precision="tf32")
+    od, oi = oracle.knn(x, 20)
+    # the distance of each returned neighbour agrees with its exact distance to TF32 accuracy
+    nrm = oracle.norms(x)
+    for i in range(0, 8000, 97):
+        for q in range(20):
+            j = idx[q, i]
+            exact = np.sqrt(oracle.lib().or_pair_d2(np.ascontiguousarray(x), 8000, 16, nrm, i, int(j)))
+            assert abs(dist[q, i] - exact) <= 2e-3 * (1 + exact) + 2e-3 * np.sqrt(nrm[i])
+    recall = np.mean([len(set(idx[:, i]) & set(oi[:, i])) / 20 for i in range(8000)])
+    assert recall > 0.99
+    assert (np.diff(dist, axis=0) >= 0).all()
