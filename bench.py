@@ -334,7 +334,8 @@ def main():
            "dtype": "f32" if a.precision == "fp32" else "tf32", "data": DATA_NOTE, "config": config_of(a),
            "fit_s": ms_step / 1e3, "knn_s": last.get("knn_ms", 0) / 1e3,
            "stages_ms": {k2: last.get(k2) for k2 in ("knn_ms", "knn_tile_ms", "density_ms", "dc_ms", "labels_ms")},
-           "rounds": last.get("rounds"), "num_cores": last.get("num_cores"), "final_k": last.get("final_k"),
+           "rounds": last.get("rounds"), "admitted_candidates": last.get("candidates"),
+           "num_cores": last.get("num_cores"), "final_k": last.get("final_k"),
            "engine_used": {1: "simt", 2: "tcgen05"}.get(last.get("engine_used"), "?"),
            "centers": centers.cpu().tolist(), "gpu_launches": launches, "clocks": clk.summary(),
            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,

@@ -378,7 +378,7 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     FDB_REQUIRE(cfg.precision == FDB200_FP32 || engine == FDB200_ENGINE_TCGEN05,
                 "TF32 distances need the tcgen05 engine");
     res.engine_used = engine;
-    const int kp = ((d + 4 + 7) / 8) * 8;
+    const int kp = tc_kp(d);
     const int exact = cfg.precision == FDB200_FP32 ? 1 : 0;
     if (engine == FDB200_ENGINE_TCGEN05) tc_prepare(ws, x, cfg.ldx, n, d, norms, U, thr, s);
 

@@ -66,24 +66,38 @@ __device__ __forceinline__ void append_keys(const TileRound& r, int p, const uin
     }
 }
 
-// Largest possible |acc - d2_ref| for a candidate that can enter point i's list, where acc is the
-// tcgen05 TF32 value of the augmented product (knn_tc.cu) and d2_ref the reference's FP32 d2:
-//   |acc - d2_ref| <= c1 |x_i||x_j| + c2 (n_i + n_j)
-//     c1: TF32 rounding of both coordinates (<= 2^-10 relative each), times the factor 2
-//     c2: FP32 accumulation of kp terms (generously 2^-21 each), the split norm's low part, and
-//         the reference's own rounding of the norms and of d2
-// and for an admissible candidate (d2_ref <= T) |x_j| <= |x_i| + sqrt(T + slack).
+// K of the tcgen05 operand rows: D coordinates + 3 norm columns + 3 ones, padded to 8
+__host__ __device__ inline int tc_kp(int d) { return ((d + 6 + 7) / 8) * 8; }
+
+// Filter bound of point i for the tcgen05 engine. The MMA sees x~ = x rounded to TF32 (nearest,
+// relative error <= 2^-11 per coordinate) and the norms of x~ split into three TF32-exact parts,
+// so acc(i, j) = |x~_i - x~_j|^2 up to FP32 accumulation. With r = |x_i - x_j| (real):
+//   |x~_i - x~_j| <= r + eps (|x_i| + |x_j|)                                  (triangle inequality)
+//   acc <= r^2 + 2 r eps (a + b) + eps^2 (a + b)^2 + acc_err + norm_err
+//   d2_ref >= r^2 - e_ref       (the reference's own FP32 rounding of n_i + n_j - 2 dot)
+// A candidate that can enter the list has d2_ref <= T, hence r <= R = sqrt(T + e_ref) and
+// b = |x_j| <= a + R, so acc <= U_i = T + E(a, R) for every such candidate: the filter never drops
+// one. acc_err allows 2^-20 of the summed term magnitudes per K-step of 8 (four times the FP32
+// truncation error of one tensor-core K-step), norm_err the fmaf-chain norm of x~.
 __device__ __forceinline__ float filter_bound(float T, float ni, int d, int kp, int exact)
 {
     if (!exact) return T;
     if (isinf(T)) return T;
     const double n = (double)ni, t = (double)T;
     const double a = sqrt(n) * (1.0 + 1e-6);
-    const double R = sqrt(t + 0x1p-10 * (n + t)) * (1.0 + 1e-6);
-    const double b = a + R;
-    const double c1 = 0x1p-8 * 1.01;
-    const double c2 = 2.5 * kp * 0x1p-21 + (2.0 * d + 8.0) * 0x1p-24 + 0x1p-19;
-    const double E = c1 * a * b + c2 * (n + b * b);
+    const double eps = 0x1p-11 * (1.0 + 0x1p-10);
+    const double c_ref = (2.0 * d + 8.0) * 0x1p-24;
+    const double c_acc = (double)(kp / 8) * 0x1p-20;
+    const double c_nrm = (d + 2.0) * 0x1p-24;
+    double R = sqrt(t), b = a + R;
+    for (int it = 0; it < 2; ++it) {
+        const double e_ref = c_ref * (n + b * b);
+        R = sqrt(t + e_ref) * (1.0 + 1e-6);
+        b = a + R;
+    }
+    const double nt_i = n * (1.0 + 0x1p-9), nt_j = b * b * (1.0 + 0x1p-9);   // norms of x~
+    const double E = c_ref * (n + b * b) + 2.0 * R * eps * (a + b) + eps * eps * (a + b) * (a + b) +
+                     c_acc * 2.0 * (nt_i + nt_j) + c_nrm * (nt_i + nt_j);
     return __double2float_ru(t + E);
 }
 

@@ -3,30 +3,29 @@
 // What it computes is exactly what knn_tile_simt computes (the reference FDS build's d2 and the
 // lexicographic admission, see knn.cu); only the way candidates are found differs:
 //
-//   1. TF32 filter on the tensor cores. Each point is stored twice, point-major, with K = D + 4
-//      padded to a multiple of 8:
-//          A row i = [-2 x_i, 1, 1, nh_i, nl_i, 0...]      B row j = [x_j, nh_j, nl_j, 1, 1, 0...]
-//      where n = fmaf-chain |x|^2 (the reference's norm), nh = n with its low 13 mantissa bits
-//      cleared (exact in TF32) and nl = n - nh. One 128 x 256 x K TF32 MMA then gives
-//      acc(i, j) ~= n_i + n_j - 2 x_i.x_j = d2(i, j) straight in TMEM, without an epilogue FMA.
-//   2. Rigorous margin. |acc - d2_ref| <= c1 |x_i||x_j| + c2 (n_i + n_j) for every pair (TF32
-//      rounding of each coordinate <= 2^-10 relative, FP32 accumulation, the reference's own
-//      rounding). For a candidate that can enter point i's list (d2_ref <= T_i), |x_j| <=
-//      |x_i| + sqrt(T_i), so the per-point bound U_i = T_i + M_i(|x_i|, T_i) never rejects it.
-//      The merge kernel computes U after every round (fdb_margin below).
-//   3. Exact refine. A pair that passes acc <= U_row or acc <= U_col is recomputed with the
-//      sequential fmaf chain from the original FP32 coordinates, which sit in the same shared
-//      memory tiles (the B tile holds x, the A tile -2x, an exact scaling), and admitted with the
-//      exact lexicographic test. Precision TF32 skips the refine and keeps d2 = max(acc, 0).
+//   1. TF32 filter on the tensor cores. Every coordinate is rounded to TF32 (nearest) once,
+//      x~ = rna(x), and each point is stored twice, point-major, K = D + 6 padded to 8:
+//          A row i = [-2 x~_i, 1, 1, 1, nh_i, nm_i, nl_i, 0...]
+//          B row j = [x~_j, nh_j, nm_j, nl_j, 1, 1, 1, 0...]
+//      with nh + nm + nl = |x~|^2 (fmaf chain) split into three TF32-exact parts. Every operand is
+//      exactly representable in TF32, so the 128 x 256 x K TF32 MMA gives
+//      acc(i, j) = |x~_i - x~_j|^2 up to FP32 accumulation, straight in TMEM.
+//   2. Rigorous margin (filter_bound in knn_common.cuh): a candidate that can still enter point
+//      i's list always has acc <= U_i, so filtering on acc <= U never changes the result.
+//   3. Exact refine. A pair passing acc <= U_row or acc <= U_col is recomputed with the sequential
+//      fmaf chain on the ORIGINAL coordinates, rebuilt bit-exactly in shared memory from x~ and
+//      the int16 residual m = bits(x) - bits(x~) (|m| <= 2^12), then admitted with the exact
+//      lexicographic test. Precision TF32 skips the refine and keeps d2 = max(acc, 0).
 //
 // Kernel shape (persistent, one CTA per SM, 320 threads):
 //   warp 0      TMA producer: A tile (128 rows, resident for a work item) and double-buffered
-//               B tiles (two 128-point blocks = 256 rows), plus per-point bounds / norms /
-//               thresholds with bulk copies; K is split into 32-byte panels (SWIZZLE_32B, K-major)
+//               B tiles (two 128-point blocks = 256 rows) in 32-byte K panels (SWIZZLE_32B,
+//               K-major), plus residual rows, bounds, norms and thresholds with bulk copies
 //   warp 1      TMEM owner and MMA issuer (one thread): K/8 tcgen05.mma kind::tf32 per tile into
 //               one of two 256-column TMEM accumulators, tcgen05.commit to an mbarrier
-//   warps 2..9  epilogue: tcgen05.ld 32 columns at a time, OR-accumulated two-sided filter,
-//               rare refine + append; release the accumulator and the B stage
+//   warps 2..9  epilogue: tcgen05.ld 32 columns at a time, OR-accumulated two-sided filter; on a
+//               hit, per-lane survivor masks drained one column per lane per step (refine +
+//               append); then release the accumulator and the B stage
 // Every mbarrier wait is bounded (about a second); on a timeout the CTA records an error code,
 // stops issuing work, frees its TMEM and returns, and the host reports the failure.
 #include "knn_common.cuh"
@@ -46,17 +45,18 @@ constexpr int kThreads = 320;
 constexpr int kEpiWarps = 8;
 constexpr int kRows = 128;               // A rows per tile
 constexpr int kCols = 256;               // B rows per tile (two blocks)
-constexpr int kMaxKp = 72;               // K panels up to 9 (D <= 68)
+constexpr int kMaxKp = 72;               // K up to 72 floats (nine 32-byte panels)
 constexpr long long kWaitCycles = 2000000000ll;   // ~1 s at 2 GHz
 constexpr float kPoisonNorm = 1.2676506002282294e30f;   // 2^100, exact in TF32
 
 struct Args {
-    int n, d, kp, T, b_lo, nb, cap, exact;
+    int n, d, kp, dm, T, b_lo, nb, cap, exact;
     int diag, delta0, ndelta, npairs, pairs_per_item, items;
     int row_pad;                 // Npad: first poison row of the B array
     const float* U;              // filter bounds (Npad + 128)
     const float* nrm;            // exact fp32 norms (Npad + 128)
     const uint64_t* thr;         // exact admission thresholds (Npad + 128)
+    const int16_t* resid;        // bits(x) - bits(x~), dm per row (Npad + 128 rows)
     uint64_t* cand;
     int* cnt;
     int* ovf;
@@ -177,10 +177,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
 // ------------------------------------------------------------------ shared memory plan
 struct Smem {
     // offsets in bytes from the 1024-aligned base
-    uint32_t a, b0, b1, arow_u, arow_n, arow_t, bcol_u[2], bcol_n[2], bcol_t[2], scratch, bars, misc, total;
+    uint32_t a, b0, b1, am, bm0, bm1, arow_u, arow_n, arow_t, bcol_u[2], bcol_n[2], bcol_t[2], bars, misc, total;
 };
 
-__host__ __device__ inline Smem smem_plan(int kp)
+// dm: residual entries per row (D rounded up to 8, so a 128-row block is a 16-byte multiple)
+__host__ __device__ inline Smem smem_plan(int kp, int dm)
 {
     Smem s;
     const uint32_t panels = (uint32_t)kp / 8;
@@ -191,6 +192,15 @@ __host__ __device__ inline Smem smem_plan(int kp)
     o += panels * kCols * 32;
     s.b1 = o;
     o += panels * kCols * 32;
+    s.am = o;                          // residuals of the A tile; the TF32-mode stash reuses it
+    o += (uint32_t)kRows * dm * 2;
+    s.bm0 = o;
+    o += (uint32_t)kCols * dm * 2;
+    s.bm1 = o;
+    o += (uint32_t)kCols * dm * 2;
+    const uint32_t stash = kEpiWarps * 32 * 33 * 4;
+    if (o - s.am < stash) o = s.am + stash;
+    o = (o + 15) & ~15u;
     s.arow_u = o;
     o += kRows * 4;
     s.arow_n = o;
@@ -205,9 +215,6 @@ __host__ __device__ inline Smem smem_plan(int kp)
         s.bcol_t[q] = o;
         o += kCols * 8;
     }
-    s.scratch = o;
-    o += kEpiWarps * 32 * 33 * 4;
-    o = (o + 15) & ~15u;
     s.bars = o;
     o += 16 * 8;
     s.misc = o;
@@ -225,20 +232,29 @@ __device__ __forceinline__ const float4* panel_chunk(const unsigned char* base, 
     return reinterpret_cast<const float4*>(base + (size_t)panel * rows_per_panel * 32 + row * 32 + phys * 16);
 }
 
-// exact d2 of (A row ra, B row rb) from the tiles: fmaf chain over d = 0..D-1
-__device__ __forceinline__ float refine_d2(const unsigned char* abase, int ra, const unsigned char* bbase, int rb,
-                                           int d, float na, float nb)
+// original coordinate from its TF32 rounding and the stored bit difference
+__device__ __forceinline__ float rebuild(float xt, int16_t m) { return __int_as_float(__float_as_int(xt) + (int)m); }
+
+// exact d2 of (A row ra, B row rb): fmaf chain over d = 0..D-1 on the rebuilt FP32 coordinates
+__device__ __forceinline__ float refine_d2(const unsigned char* abase, const int16_t* am, int ra,
+                                           const unsigned char* bbase, const int16_t* bm, int rb, int d, int dm,
+                                           float na, float nb)
 {
     float dot = 0.0f;
     const int chunks = (d + 3) >> 2;
+    const int16_t* ar = am + (size_t)ra * dm;
+    const int16_t* br = bm + (size_t)rb * dm;
     for (int c = 0; c < chunks; ++c) {
         const float4 av = *panel_chunk(abase, kRows, ra, c);
         const float4 bv = *panel_chunk(bbase, kCols, rb, c);
-        const float a4[4] = {av.x, av.y, av.z, av.w};
-        const float b4[4] = {bv.x, bv.y, bv.z, bv.w};
+        const short4 ma = *reinterpret_cast<const short4*>(ar + 4 * c);
+        const short4 mb = *reinterpret_cast<const short4*>(br + 4 * c);
+        const float xa[4] = {rebuild(__fmul_rn(-0.5f, av.x), ma.x), rebuild(__fmul_rn(-0.5f, av.y), ma.y),
+                             rebuild(__fmul_rn(-0.5f, av.z), ma.z), rebuild(__fmul_rn(-0.5f, av.w), ma.w)};
+        const float xb[4] = {rebuild(bv.x, mb.x), rebuild(bv.y, mb.y), rebuild(bv.z, mb.z), rebuild(bv.w, mb.w)};
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-            if (c * 4 + e < d) dot = __fmaf_rn(__fmul_rn(-0.5f, a4[e]), b4[e], dot);
+            if (c * 4 + e < d) dot = __fmaf_rn(xa[e], xb[e], dot);
     }
     return exact_d2(na, nb, dot);
 }
@@ -297,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    const Smem P = smem_plan(a.kp);
+    const Smem P = smem_plan(a.kp, a.dm);
     const int panels = a.kp / 8;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P.bars);
     uint64_t* a_full = bars + 0;
@@ -335,6 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const uint32_t a_bytes = (uint32_t)panels * kRows * 32;
     const uint32_t b_half_bytes = (uint32_t)panels * kRows * 32;
+    const uint32_t m_block_bytes = a.exact ? (uint32_t)kRows * a.dm * 2 : 0u;
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
@@ -344,9 +361,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
                 if (!mbar_wait(a_empty, (t & 1) ^ 1, abort_flag, a.err, 1)) { ok = false; break; }
                 const int B = a.b_lo + item % a.nb;
-                mbar_expect_tx(a_full, a_bytes + kRows * 16);
+                mbar_expect_tx(a_full, a_bytes + kRows * 16 + m_block_bytes);
                 for (int p = 0; p < panels; ++p)
                     tma_load_2d(sm + P.a + p * kRows * 32, &mapA, p * 8, B * kRows, a_full);
+                if (m_block_bytes)
+                    bulk_load(sm + P.am, a.resid + (size_t)B * kRows * a.dm, m_block_bytes, a_full);
                 bulk_load(sm + P.arow_u, a.U + (size_t)B * kRows, kRows * 4, a_full);
                 bulk_load(sm + P.arow_n, a.nrm + (size_t)B * kRows, kRows * 4, a_full);
                 bulk_load(sm + P.arow_t, a.thr + (size_t)B * kRows, kRows * 8, a_full);
@@ -357,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!mbar_wait(&b_empty[s], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 2)) { ok = false; break; }
                     const Unit u = make_unit(a, item, p_lo + uix);
                     unsigned char* bb = sm + (s ? P.b1 : P.b0);
-                    mbar_expect_tx(&b_full[s], 2 * b_half_bytes + 2 * kRows * 16);
+                    mbar_expect_tx(&b_full[s], 2 * b_half_bytes + 2 * kRows * 16 + 2 * m_block_bytes);
                     const int rows0 = (u.R0 >= 0 ? u.R0 * kRows : a.row_pad);
                     const int rows1 = (u.R1 >= 0 ? u.R1 * kRows : a.row_pad);
                     for (int p = 0; p < panels; ++p) {
@@ -370,6 +389,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     bulk_load(sm + P.bcol_n[s] + kRows * 4, a.nrm + rows1, kRows * 4, &b_full[s]);
                     bulk_load(sm + P.bcol_t[s], a.thr + rows0, kRows * 8, &b_full[s]);
                     bulk_load(sm + P.bcol_t[s] + kRows * 8, a.thr + rows1, kRows * 8, &b_full[s]);
+                    if (m_block_bytes) {
+                        unsigned char* bmd = sm + (s ? P.bm1 : P.bm0);
+                        bulk_load(bmd, a.resid + (size_t)rows0 * a.dm, m_block_bytes, &b_full[s]);
+                        bulk_load(bmd + m_block_bytes, a.resid + (size_t)rows1 * a.dm, m_block_bytes, &b_full[s]);
+                    }
                 }
             }
             // on abort, let copies already issued land before the CTA exits (bounded)
@@ -413,7 +437,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quad = warp & 3;              // TMEM lanes this warp may read
         const int half = e >> 2;                // column half of the tile
         const int ra = quad * 32 + lane;        // this thread's A row (tile-local)
-        float* scr = reinterpret_cast<float*>(sm + P.scratch) + (size_t)e * 32 * 33;
+        float* scr = reinterpret_cast<float*>(sm + P.am) + (size_t)e * 32 * 33;   // TF32 mode only
+        const int16_t* am = reinterpret_cast<const int16_t*>(sm + P.am);
         int g = 0;
         bool ok = true;
         for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
@@ -431,6 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const Unit u = make_unit(a, item, p_lo + uix);
                 const int gi = u.B * kRows + ra;
                 const unsigned char* bb = sm + (s ? P.b1 : P.b0);
+                const int16_t* bm = reinterpret_cast<const int16_t*>(sm + (s ? P.bm1 : P.bm0));
                 const float* cu = reinterpret_cast<const float*>(sm + P.bcol_u[s]);
                 const float* cn = reinterpret_cast<const float*>(sm + P.bcol_n[s]);
                 const uint64_t* ct = reinterpret_cast<const uint64_t*>(sm + P.bcol_t[s]);
@@ -439,40 +465,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int cb = half * 128 + c * 32;
                     float v[32];
                     tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(s * kCols + cb), v);
-                    bool any = false;
+                    // fast path: one OR-accumulated two-sided test per pair
+                    unsigned mrow = 0, mcol = 0;
 #pragma unroll
                     for (int q = 0; q < 32; q += 4) {
                         const float4 u4 = *reinterpret_cast<const float4*>(cu + cb + q);
-                        any |= (v[q] <= Ui) | (v[q] <= u4.x);
-                        any |= (v[q + 1] <= Ui) | (v[q + 1] <= u4.y);
-                        any |= (v[q + 2] <= Ui) | (v[q + 2] <= u4.z);
-                        any |= (v[q + 3] <= Ui) | (v[q + 3] <= u4.w);
-                    }
-                    if (!__any_sync(0xffffffffu, any)) continue;
-                    // slow path: stash the row so survivors can be visited with a dynamic index
+                        const float uc[4] = {u4.x, u4.y, u4.z, u4.w};
 #pragma unroll
-                    for (int q = 0; q < 32; ++q) scr[lane * 33 + q] = v[q];
-                    __syncwarp();
-                    if (any && gi < a.n) {
-                        for (int q = 0; q < 32; ++q) {
-                            const float acc = scr[lane * 33 + q];
-                            const float Uj = cu[cb + q];
-                            const bool row_ok = acc <= Ui;
-                            const bool col_ok = !a.diag && acc <= Uj;
-                            if (!row_ok && !col_ok) continue;
+                        for (int w = 0; w < 4; ++w) {
+                            mrow |= (v[q + w] <= Ui ? 1u : 0u) << (q + w);
+                            mcol |= (v[q + w] <= uc[w] ? 1u : 0u) << (q + w);
+                        }
+                    }
+                    if (a.diag) mcol = 0;              // diagonal units: both orders are rows
+                    if (gi >= a.n) mrow = mcol = 0;    // padding rows
+                    if (!__any_sync(0xffffffffu, (mrow | mcol) != 0u)) continue;
+                    if (!a.exact) {
+#pragma unroll
+                        for (int q = 0; q < 32; ++q) scr[lane * 33 + q] = v[q];
+                    }
+                    // drain the survivors: every lane takes its lowest remaining column per step
+                    unsigned m = mrow | mcol;
+                    while (__any_sync(0xffffffffu, m != 0u)) {
+                        if (m) {
+                            const int q = __ffs(m) - 1;
+                            m &= m - 1;
+                            const unsigned bit = 1u << q;
                             const int jloc = cb + q;
                             const int gj = rblk * kRows + c * 32 + q;
-                            if (gj == gi || gj >= a.n) continue;   // self pair / padding
-                            const float nj = cn[jloc];
-                            const float d2 = a.exact ? refine_d2(sm + P.a, ra, bb, jloc, a.d, ni, nj)
-                                                     : fmaxf(acc, 0.0f);
-                            if (row_ok) {
-                                const uint64_t key = pack_key(d2, gj);
-                                if (key < ti) tc_append(a, gi, key);
-                            }
-                            if (col_ok) {
-                                const uint64_t key = pack_key(d2, gi);
-                                if (key < ct[jloc]) tc_append(a, gj, key);
+                            if (gj != gi && gj < a.n) {
+                                const float d2 = a.exact ? refine_d2(sm + P.a, am, ra, bb, bm, jloc, a.d, a.dm, ni, cn[jloc])
+                                                         : fmaxf(scr[lane * 33 + q], 0.0f);
+                                if (mrow & bit) {
+                                    const uint64_t key = pack_key(d2, gj);
+                                    if (key < ti) tc_append(a, gi, key);
+                                }
+                                if (mcol & bit) {
+                                    const uint64_t key = pack_key(d2, gi);
+                                    if (key < ct[jloc]) tc_append(a, gj, key);
+                                }
                             }
                         }
                     }
@@ -499,44 +530,58 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ data preparation
-// A / B rows (point-major, kp floats) from the dim-major dataset; padded rows are poison.
-__global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, int d, int kp, int rows_a,
-                                  int rows_b, const float* __restrict__ norms, float* __restrict__ A,
-                                  float* __restrict__ Bm)
+__device__ __forceinline__ float rna_tf32(float x)
 {
-    const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const size_t total = (size_t)rows_b * kp;
-    if (t >= total) return;
-    const int i = (int)(t / kp), k = (int)(t % kp);
-    float va = 0.0f, vb = 0.0f;
-    if (i < n) {
-        const float nn = norms[i];
-        const float nh = __uint_as_float(__float_as_uint(nn) & 0xFFFFE000u);
-        const float nl = __fsub_rn(nn, nh);
-        if (k < d) {
-            const float xv = x[(size_t)k * ldx + i];
-            va = __fmul_rn(-2.0f, xv);
-            vb = xv;
-        } else if (k == d) {
-            va = 1.0f;
-            vb = nh;
-        } else if (k == d + 1) {
-            va = 1.0f;
-            vb = nl;
-        } else if (k == d + 2) {
-            va = nh;
-            vb = 1.0f;
-        } else if (k == d + 3) {
-            va = nl;
-            vb = 1.0f;
+    // round the magnitude to 11 significant bits, ties away from zero
+    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+
+__device__ __forceinline__ void split3(float v, float& h, float& m, float& l)
+{
+    h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+    const float r = __fsub_rn(v, h);
+    m = __uint_as_float(__float_as_uint(r) & 0xFFFFE000u);
+    l = __fsub_rn(r, m);   // at most 2 significant bits remain: exact in TF32
+}
+
+// One thread per row: TF32-rounded A / B operand rows, residuals, and poison for padding rows
+// (their product with any real row is 2^100, above every finite bound).
+__global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, int d, int kp, int dm,
+                                  int rows_a, int rows_b, float* __restrict__ A, float* __restrict__ Bm,
+                                  int16_t* __restrict__ resid)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows_b) return;
+    float* arow = (i < rows_a) ? A + (size_t)i * kp : nullptr;
+    float* brow = Bm + (size_t)i * kp;
+    int16_t* mrow = resid + (size_t)i * dm;
+    if (i >= n) {
+        for (int k = 0; k < kp; ++k) {
+            if (arow) arow[k] = (k == d + 3) ? kPoisonNorm : 0.0f;
+            brow[k] = (k == d) ? kPoisonNorm : 0.0f;
         }
-    } else {
-        // padding / poison row: its product with any real row is 2^100, above every finite bound
-        if (k == d + 2) va = kPoisonNorm;
-        if (k == d) vb = kPoisonNorm;
+        for (int k = 0; k < dm; ++k) mrow[k] = 0;
+        return;
     }
-    if (i < rows_a) A[t] = va;
-    Bm[t] = vb;
+    float nt = 0.0f;
+    for (int k = 0; k < d; ++k) {
+        const float xv = x[(size_t)k * ldx + i];
+        const float xt = rna_tf32(xv);
+        nt = __fmaf_rn(xt, xt, nt);
+        if (arow) arow[k] = __fmul_rn(-2.0f, xt);
+        brow[k] = xt;
+        mrow[k] = (int16_t)(__float_as_int(xv) - __float_as_int(xt));
+    }
+    for (int k = d; k < dm; ++k) mrow[k] = 0;
+    float h, m, l;
+    split3(nt, h, m, l);
+    const float av[6] = {1.0f, 1.0f, 1.0f, h, m, l};
+    const float bv[6] = {h, m, l, 1.0f, 1.0f, 1.0f};
+    for (int k = d; k < kp; ++k) {
+        const int o = k - d;
+        if (arow) arow[k] = (o < 6) ? av[o] : 0.0f;
+        brow[k] = (o < 6) ? bv[o] : 0.0f;
+    }
 }
 
 }  // namespace tc
@@ -573,6 +618,8 @@ struct TcState {
     int device = -1, n = 0, d = 0, kp = 0, npad = 0;
     const float* x = nullptr;
     float *A = nullptr, *B = nullptr, *U = nullptr, *nrm = nullptr;   // U/nrm/thr: scheduler-owned
+    int16_t* resid = nullptr;
+    int dm = 0;
     uint64_t* thr = nullptr;
     CUtensorMap mapA, mapB;
     int sms = 0;
@@ -588,8 +635,9 @@ bool tc_engine_supported(int d)
     if (cudaGetDevice(&dev) != cudaSuccess) return false;
     cudaDeviceProp p;
     if (cudaGetDeviceProperties(&p, dev) != cudaSuccess) return false;
-    const int kp = ((d + 4 + 7) / 8) * 8;
-    return p.major == 10 && p.minor == 0 && kp <= tc::kMaxKp && tc::smem_plan(kp).total + 1024 <= 227 * 1024;
+    const int kp = tc_kp(d);
+    const int dm = ((d + 7) / 8) * 8;
+    return p.major == 10 && p.minor == 0 && kp <= tc::kMaxKp && tc::smem_plan(kp, dm).total + 1024 <= 227 * 1024;
 }
 
 // Prepares the TF32 operand rows and tensor maps for one kNN call; the per-point bounds,
@@ -598,19 +646,21 @@ void tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const floa
                 const uint64_t* thr, cudaStream_t s)
 {
     TcState& st = g_state;
-    const int kp = ((d + 4 + 7) / 8) * 8;
+    const int kp = tc_kp(d);
+    const int dm = ((d + 7) / 8) * 8;
     const int T = (n + kBlock - 1) / kBlock;
     const int npad = T * kBlock;
     const int rows_b = npad + kBlock;     // + one poison block
     const size_t a_bytes = sizeof(float) * (size_t)npad * kp;
     const size_t b_bytes = sizeof(float) * (size_t)rows_b * kp;
-    char* mem = (char*)ws.ops.ensure(a_bytes + b_bytes + 2048);
+    const size_t m_bytes = sizeof(int16_t) * (size_t)rows_b * dm;
+    char* mem = (char*)ws.ops.ensure(a_bytes + b_bytes + m_bytes + 3072);
     auto align = [](char* p) { return (char*)(((uintptr_t)p + 1023) & ~(uintptr_t)1023); };
     st.A = (float*)align(mem);
     st.B = (float*)align((char*)st.A + a_bytes);
-    const size_t total = (size_t)rows_b * kp;
-    tc::build_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(x, ldx, n, d, kp, npad, rows_b, norms,
-                                                                          st.A, st.B);
+    st.resid = (int16_t*)align((char*)st.B + b_bytes);
+    tc::build_rows_kernel<<<(rows_b + 127) / 128, 128, 0, s>>>(x, ldx, n, d, kp, dm, npad, rows_b, st.A, st.B,
+                                                               st.resid);
     FDB_LAUNCHED();
     make_map(&st.mapA, st.A, npad, kp);
     make_map(&st.mapB, st.B, rows_b, kp);
@@ -621,6 +671,7 @@ void tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const floa
     st.n = n;
     st.d = d;
     st.kp = kp;
+    st.dm = dm;
     st.npad = npad;
     st.x = x;
     st.U = const_cast<float*>(U);
@@ -636,6 +687,8 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.n = r.n;
     a.d = r.d;
     a.kp = st.kp;
+    a.dm = st.dm;
+    a.resid = st.resid;
     a.T = r.T;
     a.b_lo = r.b_lo;
     a.nb = r.nb;
@@ -666,7 +719,7 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
         a.items = r.nb * ((a.npairs + ppi - 1) / ppi);
     }
     if (a.items <= 0) return;
-    const tc::Smem P = tc::smem_plan(st.kp);
+    const tc::Smem P = tc::smem_plan(st.kp, st.dm);
     const size_t smem = P.total + 1024;
     static bool attr_set = false;
     if (!attr_set) {
