@@ -18,7 +18,7 @@ def _exact(fdb, oracle, x, k, **kw):
 
 
 @pytest.mark.parametrize("n,d,k", [(2, 1, 1), (129, 3, 5), (300, 2, 7), (1000, 16, 20), (2049, 50, 45),
-                                   (5000, 8, 31), (3000, 52, 10), (777, 47, 30)])
+                                   (5000, 8, 31), (3000, 50, 10), (777, 47, 30)])
 def test_tc_bit_exact_small(fdb, oracle, n, d, k):
     rng = np.random.default_rng(7 * n + d)
     x = rng.uniform(-1, 1, (d, n)).astype(np.float32)
