@@ -28,6 +28,8 @@
 
 #include <algorithm>
 #include <cfloat>
+#include <cstdio>
+#include <cstdlib>
 #include <vector>
 
 namespace fdb {
@@ -395,6 +397,9 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     FDB_CUDA(cudaEventCreate(&t0));
     FDB_CUDA(cudaEventCreate(&t1));
     const int dmax = T / 2;
+    const char* trace_env = getenv("FDB200_TRACE");
+    const bool trace = trace_env && trace_env[0] == '1';
+    unsigned long long adm_before = 0;
     bool diag_done = false;
     int next_delta = 1;
     double seen = kBlock - 1;   // candidates each point has been offered so far (approximate)
@@ -450,6 +455,15 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
         knn_merge_kernel<<<(n + mwarps - 1) / mwarps, mwarps * 32, msmem, s>>>(
             lists, thr, U, norms, cand, cnt, n, k, cap, pw, d, kp, exact, admitted);
         FDB_LAUNCHED();
+        if (trace) {
+            unsigned long long adm = 0;
+            FDB_CUDA(cudaMemcpyAsync(&adm, admitted, sizeof(adm), cudaMemcpyDeviceToHost, s));
+            FDB_CUDA(cudaStreamSynchronize(s));
+            fprintf(stderr, "[fdb200] round %d %s delta0=%d ndelta=%d units=%d tile_ms=%.3f admitted=%llu (%.1f/point)\n",
+                    res.rounds, r.diag ? "diag" : "offs", r.delta0, r.diag ? 0 : ndelta, units, ms,
+                    adm - adm_before, (double)(adm - adm_before) / n);
+            adm_before = adm;
+        }
         if (!diag_done) {
             diag_done = true;
         } else {
