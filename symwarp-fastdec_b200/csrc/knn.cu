@@ -362,7 +362,7 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     float* U = ws.fthr.as<float>(rows);
     uint64_t* cand = ws.cand.as<uint64_t>((size_t)n * cap);
     int* cnt = ws.cnt.as<int>(n);
-    int* ovf = ws.flags.as<int>(16);   // [0] overflow, [1] tcgen05 error code, [2..3] admitted count
+    int* ovf = ws.flags.as<int>(16);   // [0] overflow, [1] tcgen05 error, [2..3] admitted, [8..13] trace counters
     unsigned long long* admitted = reinterpret_cast<unsigned long long*>(ovf + 2);
     compute_norms(x, cfg.ldx, n, d, norms, s);
     init_point_state_kernel<<<(rows + 255) / 256, 256, 0, s>>>(n, rows, norms, thr, U);
@@ -400,6 +400,8 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     const char* trace_env = getenv("FDB200_TRACE");
     const bool trace = trace_env && trace_env[0] == '1';
     unsigned long long adm_before = 0;
+    unsigned long long* counters = reinterpret_cast<unsigned long long*>(ovf + 8);   // flags[8..13]
+    r.counters = trace ? counters : nullptr;
     bool diag_done = false;
     int next_delta = 1;
     double seen = kBlock - 1;   // candidates each point has been offered so far (approximate)
@@ -456,12 +458,17 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
             lists, thr, U, norms, cand, cnt, n, k, cap, pw, d, kp, exact, admitted);
         FDB_LAUNCHED();
         if (trace) {
-            unsigned long long adm = 0;
+            unsigned long long adm = 0, cn[3] = {0, 0, 0};
             FDB_CUDA(cudaMemcpyAsync(&adm, admitted, sizeof(adm), cudaMemcpyDeviceToHost, s));
+            FDB_CUDA(cudaMemcpyAsync(cn, counters, sizeof(cn), cudaMemcpyDeviceToHost, s));
+            FDB_CUDA(cudaMemsetAsync(counters, 0, sizeof(cn), s));
             FDB_CUDA(cudaStreamSynchronize(s));
-            fprintf(stderr, "[fdb200] round %d %s delta0=%d ndelta=%d units=%d tile_ms=%.3f admitted=%llu (%.1f/point)\n",
+            const double chunks = (double)units * 32.0;   // 8 warps x 4 chunks per 128 x 256 tile
+            fprintf(stderr, "[fdb200] round %d %s delta0=%d ndelta=%d units=%d tile_ms=%.3f admitted=%llu (%.1f/point)"
+                            " refined=%llu (%.2f/chunk) hit_chunks=%.1f%% drain_steps/hit_chunk=%.2f\n",
                     res.rounds, r.diag ? "diag" : "offs", r.delta0, r.diag ? 0 : ndelta, units, ms,
-                    adm - adm_before, (double)(adm - adm_before) / n);
+                    adm - adm_before, (double)(adm - adm_before) / n, cn[0], cn[0] / chunks,
+                    100.0 * cn[1] / chunks, cn[1] ? (double)cn[2] / cn[1] : 0.0);
             adm_before = adm;
         }
         if (!diag_done) {

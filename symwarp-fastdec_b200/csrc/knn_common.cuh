@@ -32,6 +32,7 @@ struct TileRound {
     int diag;                // 1: diagonal units (B, B), row side only
     int delta0;              // first block offset of the round
     int ndelta;              // block offsets in the round
+    unsigned long long* counters;   // optional tcgen05 diagnostics (FDB200_TRACE=1), else null
 };
 
 __device__ __forceinline__ bool decode_unit(const TileRound& r, int u, int& B, int& R)

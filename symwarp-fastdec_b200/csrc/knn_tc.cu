@@ -61,6 +61,7 @@ struct Args {
     int* cnt;
     int* ovf;
     int* err;
+    unsigned long long* counters;   // [0] refined pairs, [1] chunks with survivors, [2] drain steps
 };
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -486,6 +487,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     // drain the survivors: every lane takes its lowest remaining column per step
                     unsigned m = mrow | mcol;
+                    if (a.counters) {
+                        unsigned tot = __popc(m);
+#pragma unroll
+                        for (int off = 16; off > 0; off >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, off);
+                        unsigned steps = __popc(m);
+#pragma unroll
+                        for (int off = 16; off > 0; off >>= 1) steps = max(steps, __shfl_xor_sync(0xffffffffu, steps, off));
+                        if (lane == 0) {
+                            atomicAdd(&a.counters[0], (unsigned long long)tot);
+                            atomicAdd(&a.counters[1], 1ull);
+                            atomicAdd(&a.counters[2], (unsigned long long)steps);
+                        }
+                    }
                     while (__any_sync(0xffffffffu, m != 0u)) {
                         if (m) {
                             const int q = __ffs(m) - 1;
@@ -705,6 +719,7 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.cnt = r.cnt;
     a.ovf = r.ovf;
     a.err = r.ovf + 1;
+    a.counters = r.counters;
     if (r.diag) {
         a.npairs = 1;
         a.pairs_per_item = 1;
