@@ -176,9 +176,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
 }
 
 // ------------------------------------------------------------------ shared memory plan
+constexpr int kQueueCap = 1024;          // survivor entries per tile queue (three queues)
+
 struct Smem {
     // offsets in bytes from the 1024-aligned base
-    uint32_t a, b0, b1, am, bm0, bm1, arow_u, arow_n, arow_t, bcol_u[2], bcol_n[2], bcol_t[2], bars, misc, total;
+    uint32_t a, b0, b1, am, bm0, bm1, arow_u, bcol_u[2], queue, qcount, bars, misc, total;
 };
 
 // dm: residual entries per row (D rounded up to 8, so a 128-row block is a 16-byte multiple)
@@ -193,29 +195,26 @@ __host__ __device__ inline Smem smem_plan(int kp, int dm)
     o += panels * kCols * 32;
     s.b1 = o;
     o += panels * kCols * 32;
-    s.am = o;                          // residuals of the A tile; the TF32-mode stash reuses it
+    s.am = o;                          // residuals of the A tile (exact mode) or queued acc (TF32 mode)
     o += (uint32_t)kRows * dm * 2;
     s.bm0 = o;
     o += (uint32_t)kCols * dm * 2;
     s.bm1 = o;
     o += (uint32_t)kCols * dm * 2;
-    const uint32_t stash = kEpiWarps * 32 * 33 * 4;
-    if (o - s.am < stash) o = s.am + stash;
+    // TF32 mode: queued acc values plus the in-place drain stash of every epilogue warp
+    const uint32_t accq = 3u * kQueueCap * 4u + kEpiWarps * 32 * 33 * 4;
+    if (o - s.am < accq) o = s.am + accq;
     o = (o + 15) & ~15u;
     s.arow_u = o;
     o += kRows * 4;
-    s.arow_n = o;
-    o += kRows * 4;
-    s.arow_t = o;
-    o += kRows * 8;
     for (int q = 0; q < 2; ++q) {
         s.bcol_u[q] = o;
         o += kCols * 4;
-        s.bcol_n[q] = o;
-        o += kCols * 4;
-        s.bcol_t[q] = o;
-        o += kCols * 8;
     }
+    s.queue = o;
+    o += 3u * kQueueCap * 4u;
+    s.qcount = o;
+    o += 16;
     s.bars = o;
     o += 16 * 8;
     s.misc = o;
@@ -323,6 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* b_empty = bars + 4;     // [2]
     uint64_t* acc_full = bars + 6;    // [2]
     uint64_t* acc_empty = bars + 8;   // [2]
+    uint64_t* epi_bar = bars + 10;    // the 8 epilogue warps, once per tile
     volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + P.misc);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + P.misc + 16);
 
@@ -336,6 +336,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&acc_full[s], 1);
             mbar_init(&acc_empty[s], kEpiWarps);
         }
+        mbar_init(epi_bar, kEpiWarps);
+        int* qc = reinterpret_cast<int*>(sm + P.qcount);
+        qc[0] = qc[1] = qc[2] = 0;
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -362,14 +365,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
                 if (!mbar_wait(a_empty, (t & 1) ^ 1, abort_flag, a.err, 1)) { ok = false; break; }
                 const int B = a.b_lo + item % a.nb;
-                mbar_expect_tx(a_full, a_bytes + kRows * 16 + m_block_bytes);
+                mbar_expect_tx(a_full, a_bytes + kRows * 4 + m_block_bytes);
                 for (int p = 0; p < panels; ++p)
                     tma_load_2d(sm + P.a + p * kRows * 32, &mapA, p * 8, B * kRows, a_full);
                 if (m_block_bytes)
                     bulk_load(sm + P.am, a.resid + (size_t)B * kRows * a.dm, m_block_bytes, a_full);
                 bulk_load(sm + P.arow_u, a.U + (size_t)B * kRows, kRows * 4, a_full);
-                bulk_load(sm + P.arow_n, a.nrm + (size_t)B * kRows, kRows * 4, a_full);
-                bulk_load(sm + P.arow_t, a.thr + (size_t)B * kRows, kRows * 8, a_full);
                 int p_lo;
                 const int nu = item_units(a, item, p_lo);
                 for (int uix = 0; uix < nu; ++uix, ++g) {
@@ -377,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!mbar_wait(&b_empty[s], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 2)) { ok = false; break; }
                     const Unit u = make_unit(a, item, p_lo + uix);
                     unsigned char* bb = sm + (s ? P.b1 : P.b0);
-                    mbar_expect_tx(&b_full[s], 2 * b_half_bytes + 2 * kRows * 16 + 2 * m_block_bytes);
+                    mbar_expect_tx(&b_full[s], 2 * b_half_bytes + 2 * kRows * 4 + 2 * m_block_bytes);
                     const int rows0 = (u.R0 >= 0 ? u.R0 * kRows : a.row_pad);
                     const int rows1 = (u.R1 >= 0 ? u.R1 * kRows : a.row_pad);
                     for (int p = 0; p < panels; ++p) {
@@ -386,10 +387,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     bulk_load(sm + P.bcol_u[s], a.U + rows0, kRows * 4, &b_full[s]);
                     bulk_load(sm + P.bcol_u[s] + kRows * 4, a.U + rows1, kRows * 4, &b_full[s]);
-                    bulk_load(sm + P.bcol_n[s], a.nrm + rows0, kRows * 4, &b_full[s]);
-                    bulk_load(sm + P.bcol_n[s] + kRows * 4, a.nrm + rows1, kRows * 4, &b_full[s]);
-                    bulk_load(sm + P.bcol_t[s], a.thr + rows0, kRows * 8, &b_full[s]);
-                    bulk_load(sm + P.bcol_t[s] + kRows * 8, a.thr + rows1, kRows * 8, &b_full[s]);
                     if (m_block_bytes) {
                         unsigned char* bmd = sm + (s ? P.bm1 : P.bm0);
                         bulk_load(bmd, a.resid + (size_t)rows0 * a.dm, m_block_bytes, &b_full[s]);
@@ -438,98 +435,161 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quad = warp & 3;              // TMEM lanes this warp may read
         const int half = e >> 2;                // column half of the tile
         const int ra = quad * 32 + lane;        // this thread's A row (tile-local)
-        float* scr = reinterpret_cast<float*>(sm + P.am) + (size_t)e * 32 * 33;   // TF32 mode only
         const int16_t* am = reinterpret_cast<const int16_t*>(sm + P.am);
+        uint32_t* queues = reinterpret_cast<uint32_t*>(sm + P.queue);
+        float* qacc = reinterpret_cast<float*>(sm + P.am);          // TF32 mode: acc of queued pairs
+        int* qcount = reinterpret_cast<int*>(sm + P.qcount);
         int g = 0;
         bool ok = true;
         for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
             if (!mbar_wait(a_full, t & 1, abort_flag, a.err, 6)) { ok = false; break; }
-            const float* au = reinterpret_cast<const float*>(sm + P.arow_u);
-            const float Ui = au[ra];
-            const float ni = reinterpret_cast<const float*>(sm + P.arow_n)[ra];
-            const uint64_t ti = reinterpret_cast<const uint64_t*>(sm + P.arow_t)[ra];
+            const float Ui = reinterpret_cast<const float*>(sm + P.arow_u)[ra];
             int p_lo;
             const int nu = item_units(a, item, p_lo);
             for (int uix = 0; uix < nu; ++uix, ++g) {
-                const int s = g & 1;
+                const int s = g & 1, qi = g % 3;
                 if (!mbar_wait(&acc_full[s], (g >> 1) & 1, abort_flag, a.err, 7)) { ok = false; break; }
                 tc_fence_after();
                 const Unit u = make_unit(a, item, p_lo + uix);
                 const int gi = u.B * kRows + ra;
+                const bool row_real = gi < a.n;
                 const unsigned char* bb = sm + (s ? P.b1 : P.b0);
                 const int16_t* bm = reinterpret_cast<const int16_t*>(sm + (s ? P.bm1 : P.bm0));
                 const float* cu = reinterpret_cast<const float*>(sm + P.bcol_u[s]);
-                const float* cn = reinterpret_cast<const float*>(sm + P.bcol_n[s]);
-                const uint64_t* ct = reinterpret_cast<const uint64_t*>(sm + P.bcol_t[s]);
+                uint32_t* queue = queues + qi * kQueueCap;
+                float* qa = qacc + qi * kQueueCap;
                 const int rblk = half ? u.R1 : u.R0;
+                // ---- phase 1: filter the accumulator, queue the survivors
                 for (int c = 0; c < 4 && rblk >= 0; ++c) {
                     const int cb = half * 128 + c * 32;
                     float v[32];
                     tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(s * kCols + cb), v);
-                    // fast path: one OR-accumulated two-sided test per pair
-                    unsigned mrow = 0, mcol = 0;
+                    float uc[32];
 #pragma unroll
                     for (int q = 0; q < 32; q += 4) {
                         const float4 u4 = *reinterpret_cast<const float4*>(cu + cb + q);
-                        const float uc[4] = {u4.x, u4.y, u4.z, u4.w};
-#pragma unroll
-                        for (int w = 0; w < 4; ++w) {
-                            mrow |= (v[q + w] <= Ui ? 1u : 0u) << (q + w);
-                            mcol |= (v[q + w] <= uc[w] ? 1u : 0u) << (q + w);
-                        }
+                        uc[q] = u4.x;
+                        uc[q + 1] = u4.y;
+                        uc[q + 2] = u4.z;
+                        uc[q + 3] = u4.w;
                     }
-                    if (a.diag) mcol = 0;              // diagonal units: both orders are rows
-                    if (gi >= a.n) mrow = mcol = 0;    // padding rows
-                    if (!__any_sync(0xffffffffu, (mrow | mcol) != 0u)) continue;
-                    if (!a.exact) {
+                    bool rh = false, ch = false;
 #pragma unroll
-                        for (int q = 0; q < 32; ++q) scr[lane * 33 + q] = v[q];
+                    for (int q = 0; q < 32; ++q) {
+                        rh = rh || (v[q] <= Ui);
+                        ch = ch || (v[q] <= uc[q]);
                     }
-                    // drain the survivors: every lane takes its lowest remaining column per step
+                    rh = rh && row_real;
+                    ch = ch && row_real && !a.diag;   // diagonal units: both orders are rows
+                    if (!__any_sync(0xffffffffu, rh || ch)) continue;
+                    unsigned mrow = 0, mcol = 0;
+                    if (rh) {
+#pragma unroll
+                        for (int q = 0; q < 32; ++q) mrow |= (v[q] <= Ui ? 1u : 0u) << q;
+                    }
+                    if (ch) {
+#pragma unroll
+                        for (int q = 0; q < 32; ++q) mcol |= (v[q] <= uc[q] ? 1u : 0u) << q;
+                    }
                     unsigned m = mrow | mcol;
-                    if (a.counters) {
-                        unsigned tot = __popc(m);
+                    const int mine = __popc(m);
+                    int incl = mine;
 #pragma unroll
-                        for (int off = 16; off > 0; off >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, off);
-                        unsigned steps = __popc(m);
-#pragma unroll
-                        for (int off = 16; off > 0; off >>= 1) steps = max(steps, __shfl_xor_sync(0xffffffffu, steps, off));
-                        if (lane == 0) {
-                            atomicAdd(&a.counters[0], (unsigned long long)tot);
-                            atomicAdd(&a.counters[1], 1ull);
-                            atomicAdd(&a.counters[2], (unsigned long long)steps);
-                        }
+                    for (int off = 1; off < 32; off <<= 1) {
+                        const int o = __shfl_up_sync(0xffffffffu, incl, off);
+                        if (lane >= off) incl += o;
                     }
-                    while (__any_sync(0xffffffffu, m != 0u)) {
-                        if (m) {
+                    const int total = __shfl_sync(0xffffffffu, incl, 31);
+                    int base = 0;
+                    if (lane == 0) base = atomicAdd(&qcount[qi], total);
+                    base = __shfl_sync(0xffffffffu, base, 0);
+                    if (a.counters && lane == 0) {
+                        atomicAdd(&a.counters[0], (unsigned long long)total);
+                        atomicAdd(&a.counters[1], 1ull);
+                    }
+                    if (base + total <= kQueueCap) {
+                        int pos = base + incl - mine;
+                        while (m) {
                             const int q = __ffs(m) - 1;
                             m &= m - 1;
                             const unsigned bit = 1u << q;
-                            const int jloc = cb + q;
-                            const int gj = rblk * kRows + c * 32 + q;
-                            if (gj != gi && gj < a.n) {
-                                const float d2 = a.exact ? refine_d2(sm + P.a, am, ra, bb, bm, jloc, a.d, a.dm, ni, cn[jloc])
-                                                         : fmaxf(scr[lane * 33 + q], 0.0f);
-                                if (mrow & bit) {
-                                    const uint64_t key = pack_key(d2, gj);
-                                    if (key < ti) tc_append(a, gi, key);
-                                }
-                                if (mcol & bit) {
-                                    const uint64_t key = pack_key(d2, gi);
-                                    if (key < ct[jloc]) tc_append(a, gj, key);
+                            queue[pos] = (uint32_t)ra | ((uint32_t)(cb + q) << 8) | ((mrow & bit) ? 1u << 16 : 0u) |
+                                         ((mcol & bit) ? 1u << 17 : 0u);
+                            ++pos;
+                        }
+                        if (!a.exact) {
+                            // TF32 mode keeps acc itself: store it with a static index
+                            int p2 = base + incl - mine;
+#pragma unroll
+                            for (int q = 0; q < 32; ++q)
+                                if ((mrow | mcol) & (1u << q)) qa[p2++] = v[q];
+                        }
+                    } else {
+                        // queue full (early rounds): drain this chunk in place, one column per lane per step
+                        if (!a.exact) {
+                            float* scr = qacc + 3 * kQueueCap + e * 32 * 33;
+#pragma unroll
+                            for (int q = 0; q < 32; ++q) scr[lane * 33 + q] = v[q];
+                        }
+                        while (__any_sync(0xffffffffu, m != 0u)) {
+                            if (m) {
+                                const int q = __ffs(m) - 1;
+                                m &= m - 1;
+                                const unsigned bit = 1u << q;
+                                const int jloc = cb + q;
+                                const int gj = rblk * kRows + c * 32 + q;
+                                if (gj != gi && gj < a.n) {
+                                    const float d2 = a.exact
+                                        ? refine_d2(sm + P.a, am, ra, bb, bm, jloc, a.d, a.dm, a.nrm[gi], a.nrm[gj])
+                                        : fmaxf(qacc[3 * kQueueCap + e * 32 * 33 + lane * 33 + q], 0.0f);
+                                    if (mrow & bit) {
+                                        const uint64_t key = pack_key(d2, gj);
+                                        if (key < a.thr[gi]) tc_append(a, gi, key);
+                                    }
+                                    if (mcol & bit) {
+                                        const uint64_t key = pack_key(d2, gi);
+                                        if (key < a.thr[gj]) tc_append(a, gj, key);
+                                    }
                                 }
                             }
                         }
                     }
                     __syncwarp();
                 }
+                // the accumulator is no longer needed: let the MMA of a later tile reuse it
                 tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[s]);
+                // queue (g + 1) % 3 last served tile g - 2, which every warp finished before the
+                // previous barrier; reset it before this barrier so tile g + 1 starts empty
+                if (e == 0 && lane == 0) qcount[(g + 1) % 3] = 0;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(epi_bar);
+                if (!mbar_wait(epi_bar, g & 1, abort_flag, a.err, 8)) { ok = false; break; }
+                // ---- phase 2: refine the queued pairs, all lanes busy
+                const int nq = min(qcount[qi], kQueueCap);
+                for (int ei = e * 32 + lane; ei < nq; ei += 256) {
+                    const uint32_t ent = queue[ei];
+                    const int qa_row = ent & 0xFF, jloc = (ent >> 8) & 0xFF;
+                    const int gi2 = u.B * kRows + qa_row;
+                    const int rb2 = (jloc < kRows) ? u.R0 : u.R1;
+                    const int gj = rb2 * kRows + (jloc & (kRows - 1));
+                    if (gj == gi2 || gj >= a.n) continue;
+                    const float d2 = a.exact
+                        ? refine_d2(sm + P.a, am, qa_row, bb, bm, jloc, a.d, a.dm, a.nrm[gi2], a.nrm[gj])
+                        : fmaxf(qacc[qi * kQueueCap + ei], 0.0f);
+                    if (ent & (1u << 16)) {
+                        const uint64_t key = pack_key(d2, gj);
+                        if (key < a.thr[gi2]) tc_append(a, gi2, key);
+                    }
+                    if (ent & (1u << 17)) {
+                        const uint64_t key = pack_key(d2, gi2);
+                        if (key < a.thr[gj]) tc_append(a, gj, key);
+                    }
+                }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&acc_empty[s]);
-                    mbar_arrive(&b_empty[s]);
-                }
+                if (lane == 0) mbar_arrive(&b_empty[s]);
             }
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(a_empty);
