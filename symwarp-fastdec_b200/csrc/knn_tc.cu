@@ -213,8 +213,8 @@ __host__ __device__ inline Smem smem_plan(int kp, int dm)
     }
     s.queue = o;
     o += 3u * kQueueCap * 4u;
-    s.qcount = o;
-    o += 16;
+    s.qcount = o;                      // [0..2] reserved entries, [4..6] end of the written prefix
+    o += 32;
     s.bars = o;
     o += 16 * 8;
     s.misc = o;
@@ -339,6 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(epi_bar, kEpiWarps);
         int* qc = reinterpret_cast<int*>(sm + P.qcount);
         qc[0] = qc[1] = qc[2] = 0;
+        qc[4] = qc[5] = qc[6] = kQueueCap;
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -525,7 +526,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 if ((mrow | mcol) & (1u << q)) qa[p2++] = v[q];
                         }
                     } else {
-                        // queue full (early rounds): drain this chunk in place, one column per lane per step
+                        // queue full (early rounds): reservations are granted in order, so entries are
+                        // valid up to the first failed one; this chunk drains in place instead
+                        if (lane == 0) atomicMin(&qcount[4 + qi], base);
                         if (!a.exact) {
                             float* scr = qacc + 3 * kQueueCap + e * 32 * 33;
 #pragma unroll
@@ -562,12 +565,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) mbar_arrive(&acc_empty[s]);
                 // queue (g + 1) % 3 last served tile g - 2, which every warp finished before the
                 // previous barrier; reset it before this barrier so tile g + 1 starts empty
-                if (e == 0 && lane == 0) qcount[(g + 1) % 3] = 0;
+                if (e == 0 && lane == 0) {
+                    qcount[(g + 1) % 3] = 0;
+                    qcount[4 + (g + 1) % 3] = kQueueCap;
+                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(epi_bar);
                 if (!mbar_wait(epi_bar, g & 1, abort_flag, a.err, 8)) { ok = false; break; }
                 // ---- phase 2: refine the queued pairs, all lanes busy
-                const int nq = min(qcount[qi], kQueueCap);
+                const int nq = min(qcount[qi], qcount[4 + qi]);
                 for (int ei = e * 32 + lane; ei < nq; ei += 256) {
                     const uint32_t ent = queue[ei];
                     const int qa_row = ent & 0xFF, jloc = (ent >> 8) & 0xFF;
