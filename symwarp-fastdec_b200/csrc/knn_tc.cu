@@ -18,9 +18,10 @@
 //      lexicographic test. Precision TF32 skips the refine and keeps d2 = max(acc, 0).
 //
 // Kernel shape (persistent, one CTA per SM, 320 threads):
-//   warp 0      TMA producer: A tile (128 rows, resident for a work item) and double-buffered
-//               B tiles (two 128-point blocks = 256 rows) in 32-byte K panels (SWIZZLE_32B,
-//               K-major), plus residual rows, bounds, norms and thresholds with bulk copies
+//   warp 0      producer: bulk copies (cp.async.bulk) of the A tile (128 rows, resident for a work
+//               item) and double-buffered B tiles (two 128-point blocks = 256 rows), stored in
+//               global memory as pre-swizzled 4 KB K panels (the SWIZZLE_32B K-major layout), plus
+//               residual rows and filter bounds
 //   warp 1      TMEM owner and MMA issuer (one thread): K/8 tcgen05.mma kind::tf32 per tile into
 //               one of two 256-column TMEM accumulators, tcgen05.commit to an mbarrier
 //   warps 2..9  epilogue: tcgen05.ld 32 columns at a time, OR-accumulated two-sided filter; on a
@@ -30,8 +31,6 @@
 // stops issuing work, frees its TMEM and returns, and the host reports the failure.
 #include "knn_common.cuh"
 
-#include <cuda.h>
-#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cmath>
@@ -57,6 +56,8 @@ struct Args {
     const float* nrm;            // exact fp32 norms (Npad + 128)
     const uint64_t* thr;         // exact admission thresholds (Npad + 128)
     const int16_t* resid;        // bits(x) - bits(x~), dm per row (Npad + 128 rows)
+    const unsigned char* aimg;   // A operand: per 128-row block, K/8 pre-swizzled 4 KB panels
+    const unsigned char* bimg;   // B operand, same layout (Npad + 128 rows)
     uint64_t* cand;
     int* cnt;
     int* ovf;
@@ -108,14 +109,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile
     return true;
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
-{
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            su32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(su32(bar))
-        : "memory");
-}
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
 {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -308,8 +301,7 @@ __device__ __forceinline__ void tc_append(const Args& a, int p, uint64_t key)
     else atomicOr(a.ovf, 1);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-    knn_tile_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, Args a)
+__global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -367,8 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!mbar_wait(a_empty, (t & 1) ^ 1, abort_flag, a.err, 1)) { ok = false; break; }
                 const int B = a.b_lo + item % a.nb;
                 mbar_expect_tx(a_full, a_bytes + kRows * 4 + m_block_bytes);
-                for (int p = 0; p < panels; ++p)
-                    tma_load_2d(sm + P.a + p * kRows * 32, &mapA, p * 8, B * kRows, a_full);
+                bulk_load(sm + P.a, a.aimg + (size_t)B * a_bytes, a_bytes, a_full);
                 if (m_block_bytes)
                     bulk_load(sm + P.am, a.resid + (size_t)B * kRows * a.dm, m_block_bytes, a_full);
                 bulk_load(sm + P.arow_u, a.U + (size_t)B * kRows, kRows * 4, a_full);
@@ -382,9 +373,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_expect_tx(&b_full[s], 2 * b_half_bytes + 2 * kRows * 4 + 2 * m_block_bytes);
                     const int rows0 = (u.R0 >= 0 ? u.R0 * kRows : a.row_pad);
                     const int rows1 = (u.R1 >= 0 ? u.R1 * kRows : a.row_pad);
+                    const unsigned char* img0 = a.bimg + (size_t)(rows0 / kRows) * b_half_bytes;
+                    const unsigned char* img1 = a.bimg + (size_t)(rows1 / kRows) * b_half_bytes;
                     for (int p = 0; p < panels; ++p) {
-                        tma_load_2d(bb + p * kCols * 32, &mapB, p * 8, rows0, &b_full[s]);
-                        tma_load_2d(bb + p * kCols * 32 + kRows * 32, &mapB, p * 8, rows1, &b_full[s]);
+                        bulk_load(bb + p * kCols * 32, img0 + p * kRows * 32, kRows * 32, &b_full[s]);
+                        bulk_load(bb + p * kCols * 32 + kRows * 32, img1 + p * kRows * 32, kRows * 32, &b_full[s]);
                     }
                     bulk_load(sm + P.bcol_u[s], a.U + rows0, kRows * 4, &b_full[s]);
                     bulk_load(sm + P.bcol_u[s] + kRows * 4, a.U + rows1, kRows * 4, &b_full[s]);
@@ -624,21 +617,31 @@ __device__ __forceinline__ void split3(float v, float& h, float& m, float& l)
     l = __fsub_rn(r, m);   // at most 2 significant bits remain: exact in TF32
 }
 
+// byte offset of element k of row i inside a blocked, pre-swizzled operand image: 128-row blocks
+// of K/8 panels, each panel 128 rows x 32 bytes with the SWIZZLE_32B chunk order, so one contiguous
+// bulk copy of a panel lands in shared memory exactly as the MMA descriptor expects it
+__device__ __forceinline__ size_t image_offset(int i, int k, int kp)
+{
+    const int blk = i >> 7, r = i & 127, p = k >> 3, c = k & 7;
+    const int phys = ((c >> 2) ^ ((r >> 2) & 1));
+    return (size_t)blk * (kp / 8) * 4096 + (size_t)p * 4096 + (size_t)r * 32 + phys * 16 + (c & 3) * 4;
+}
+
 // One thread per row: TF32-rounded A / B operand rows, residuals, and poison for padding rows
 // (their product with any real row is 2^100, above every finite bound).
 __global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, int d, int kp, int dm,
-                                  int rows_a, int rows_b, float* __restrict__ A, float* __restrict__ Bm,
-                                  int16_t* __restrict__ resid)
+                                  int rows_a, int rows_b, unsigned char* __restrict__ A,
+                                  unsigned char* __restrict__ Bm, int16_t* __restrict__ resid)
 {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= rows_b) return;
-    float* arow = (i < rows_a) ? A + (size_t)i * kp : nullptr;
-    float* brow = Bm + (size_t)i * kp;
+    const bool has_a = i < rows_a;
     int16_t* mrow = resid + (size_t)i * dm;
+    auto put = [&](unsigned char* img, int k, float v) { *reinterpret_cast<float*>(img + image_offset(i, k, kp)) = v; };
     if (i >= n) {
         for (int k = 0; k < kp; ++k) {
-            if (arow) arow[k] = (k == d + 3) ? kPoisonNorm : 0.0f;
-            brow[k] = (k == d) ? kPoisonNorm : 0.0f;
+            if (has_a) put(A, k, (k == d + 3) ? kPoisonNorm : 0.0f);
+            put(Bm, k, (k == d) ? kPoisonNorm : 0.0f);
         }
         for (int k = 0; k < dm; ++k) mrow[k] = 0;
         return;
@@ -648,8 +651,8 @@ __global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, i
         const float xv = x[(size_t)k * ldx + i];
         const float xt = rna_tf32(xv);
         nt = __fmaf_rn(xt, xt, nt);
-        if (arow) arow[k] = __fmul_rn(-2.0f, xt);
-        brow[k] = xt;
+        if (has_a) put(A, k, __fmul_rn(-2.0f, xt));
+        put(Bm, k, xt);
         mrow[k] = (int16_t)(__float_as_int(xv) - __float_as_int(xt));
     }
     for (int k = d; k < dm; ++k) mrow[k] = 0;
@@ -659,8 +662,8 @@ __global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, i
     const float bv[6] = {h, m, l, 1.0f, 1.0f, 1.0f};
     for (int k = d; k < kp; ++k) {
         const int o = k - d;
-        if (arow) arow[k] = (o < 6) ? av[o] : 0.0f;
-        brow[k] = (o < 6) ? bv[o] : 0.0f;
+        if (has_a) put(A, k, (o < 6) ? av[o] : 0.0f);
+        put(Bm, k, (o < 6) ? bv[o] : 0.0f);
     }
 }
 
@@ -669,31 +672,6 @@ __global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, i
 // ------------------------------------------------------------------ host side
 namespace {
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
-{
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (!fn) {
-        cudaDriverEntryPointQueryResult q;
-        void* p = nullptr;
-        FDB_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
-        if (q != cudaDriverEntryPointSuccess || !p) throw Error(FDB200_ECUDA, "cuTensorMapEncodeTiled unavailable");
-        fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
-    }
-    return fn;
-}
-
-void make_map(CUtensorMap* m, const float* base, int rows, int kp)
-{
-    const cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)kp * 4};
-    const cuuint32_t box[2] = {8, (cuuint32_t)tc::kRows};
-    const cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) throw Error(FDB200_ECUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
-}
-
 struct TcState {
     int device = -1, n = 0, d = 0, kp = 0, npad = 0;
     const float* x = nullptr;
@@ -701,7 +679,6 @@ struct TcState {
     int16_t* resid = nullptr;
     int dm = 0;
     uint64_t* thr = nullptr;
-    CUtensorMap mapA, mapB;
     int sms = 0;
 };
 
@@ -739,11 +716,10 @@ void tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const floa
     st.A = (float*)align(mem);
     st.B = (float*)align((char*)st.A + a_bytes);
     st.resid = (int16_t*)align((char*)st.B + b_bytes);
-    tc::build_rows_kernel<<<(rows_b + 127) / 128, 128, 0, s>>>(x, ldx, n, d, kp, dm, npad, rows_b, st.A, st.B,
-                                                               st.resid);
+    // the images have no gaps: every element is written by the build kernel
+    tc::build_rows_kernel<<<(rows_b + 127) / 128, 128, 0, s>>>(x, ldx, n, d, kp, dm, npad, rows_b,
+                                                               (unsigned char*)st.A, (unsigned char*)st.B, st.resid);
     FDB_LAUNCHED();
-    make_map(&st.mapA, st.A, npad, kp);
-    make_map(&st.mapB, st.B, rows_b, kp);
     int dev = 0;
     FDB_CUDA(cudaGetDevice(&dev));
     FDB_CUDA(cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev));
@@ -769,6 +745,8 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.kp = st.kp;
     a.dm = st.dm;
     a.resid = st.resid;
+    a.aimg = (const unsigned char*)st.A;
+    a.bimg = (const unsigned char*)st.B;
     a.T = r.T;
     a.b_lo = r.b_lo;
     a.nb = r.nb;
@@ -808,7 +786,7 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
         attr_set = true;
     }
     const int grid = std::min(a.items, st.sms);
-    tc::knn_tile_tc<<<grid, tc::kThreads, smem, s>>>(st.mapA, st.mapB, a);
+    tc::knn_tile_tc<<<grid, tc::kThreads, smem, s>>>(a);
     FDB_LAUNCHED();
 }
 
