@@ -400,8 +400,9 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     const char* trace_env = getenv("FDB200_TRACE");
     const bool trace = trace_env && trace_env[0] == '1';
     unsigned long long adm_before = 0;
-    unsigned long long* counters = reinterpret_cast<unsigned long long*>(ovf + 8);   // flags[8..13]
+    unsigned long long* counters = ws.misc2.as<unsigned long long>(16);   // trace counters
     r.counters = trace ? counters : nullptr;
+    if (trace) FDB_CUDA(cudaMemsetAsync(counters, 0, 16 * sizeof(unsigned long long), s));
     bool diag_done = false;
     int next_delta = 1;
     double seen = kBlock - 1;   // candidates each point has been offered so far (approximate)
@@ -458,7 +459,7 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
             lists, thr, U, norms, cand, cnt, n, k, cap, pw, d, kp, exact, admitted);
         FDB_LAUNCHED();
         if (trace) {
-            unsigned long long adm = 0, cn[3] = {0, 0, 0};
+            unsigned long long adm = 0, cn[16] = {0};
             FDB_CUDA(cudaMemcpyAsync(&adm, admitted, sizeof(adm), cudaMemcpyDeviceToHost, s));
             FDB_CUDA(cudaMemcpyAsync(cn, counters, sizeof(cn), cudaMemcpyDeviceToHost, s));
             FDB_CUDA(cudaMemsetAsync(counters, 0, sizeof(cn), s));
@@ -470,6 +471,15 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
                     adm - adm_before, (double)(adm - adm_before) / n, cn[0], cn[0] / chunks,
                     100.0 * cn[1] / chunks, cn[1] ? (double)cn[2] / cn[1] : 0.0);
             adm_before = adm;
+            if (engine == FDB200_ENGINE_TCGEN05 && !r.diag) {
+                // per tcgen05 tile (= two offsets), cycles per CTA role instance
+                const double tiles = (double)units / 2.0;
+                const double per_ep = tiles * 8.0;   // epilogue warp-tiles
+                fprintf(stderr, "[fdb200]   cycles/tile: prod wait A %.0f B %.0f | mma wait A %.0f B %.0f acc %.0f |"
+                                " epi wait acc %.0f filter %.0f bar %.0f refine %.0f\n",
+                        cn[4] / tiles, cn[5] / tiles, cn[6] / tiles, cn[7] / tiles, cn[8] / tiles, cn[9] / per_ep,
+                        cn[10] / per_ep, cn[11] / per_ep, cn[12] / per_ep);
+            }
         }
         if (!diag_done) {
             diag_done = true;

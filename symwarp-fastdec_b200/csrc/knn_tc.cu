@@ -93,6 +93,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity)
     return ok != 0;
 }
 
+// trace-mode phase timers: cycles accumulated per role, added to counters[4 + slot] at the end
+enum {
+    kTProdWaitA, kTProdWaitB, kTMmaWaitA, kTMmaWaitB, kTMmaWaitAcc, kTEpiWaitAcc, kTEpiP1, kTEpiBar, kTEpiP2,
+    kTNum
+};
+
 // bounded wait: false on timeout or when another role aborted the CTA
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err,
                                           int code)
@@ -355,8 +361,11 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
         if (lane == 0) {
             int g = 0;
             bool ok = true;
+            long long tw[2] = {0, 0};
             for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
+                long long c0 = clock64();
                 if (!mbar_wait(a_empty, (t & 1) ^ 1, abort_flag, a.err, 1)) { ok = false; break; }
+                tw[0] += clock64() - c0;
                 const int B = a.b_lo + item % a.nb;
                 mbar_expect_tx(a_full, a_bytes + kRows * 4 + m_block_bytes);
                 bulk_load(sm + P.a, a.aimg + (size_t)B * a_bytes, a_bytes, a_full);
@@ -367,7 +376,9 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                 const int nu = item_units(a, item, p_lo);
                 for (int uix = 0; uix < nu; ++uix, ++g) {
                     const int s = g & 1;
+                    c0 = clock64();
                     if (!mbar_wait(&b_empty[s], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 2)) { ok = false; break; }
+                    tw[1] += clock64() - c0;
                     const Unit u = make_unit(a, item, p_lo + uix);
                     unsigned char* bb = sm + (s ? P.b1 : P.b0);
                     mbar_expect_tx(&b_full[s], 2 * b_half_bytes + 2 * kRows * 4 + 2 * m_block_bytes);
@@ -388,6 +399,10 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                     }
                 }
             }
+            if (a.counters) {
+                atomicAdd(&a.counters[4 + kTProdWaitA], (unsigned long long)tw[0]);
+                atomicAdd(&a.counters[4 + kTProdWaitB], (unsigned long long)tw[1]);
+            }
             // on abort, let copies already issued land before the CTA exits (bounded)
             if (!ok) {
                 const long long t0 = clock64();
@@ -404,14 +419,21 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
         if (lane == 0) {
             int g = 0;
             bool ok = true;
+            long long tw[3] = {0, 0, 0};
             for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
+                long long c0 = clock64();
                 if (!mbar_wait(a_full, t & 1, abort_flag, a.err, 3)) { ok = false; break; }
+                tw[0] += clock64() - c0;
                 int p_lo;
                 const int nu = item_units(a, item, p_lo);
                 for (int uix = 0; uix < nu; ++uix, ++g) {
                     const int s = g & 1;
+                    c0 = clock64();
                     if (!mbar_wait(&b_full[s], (g >> 1) & 1, abort_flag, a.err, 4)) { ok = false; break; }
+                    long long c1 = clock64();
+                    tw[1] += c1 - c0;
                     if (!mbar_wait(&acc_empty[s], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 5)) { ok = false; break; }
+                    tw[2] += clock64() - c1;
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + (uint32_t)(s * kCols);
                     const uint32_t abase = su32(sm + P.a), bbase = su32(sm + (s ? P.b1 : P.b0));
@@ -420,6 +442,11 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                                  p > 0 ? 1u : 0u);
                     mma_commit(&acc_full[s]);
                 }
+            }
+            if (a.counters) {
+                atomicAdd(&a.counters[4 + kTMmaWaitA], (unsigned long long)tw[0]);
+                atomicAdd(&a.counters[4 + kTMmaWaitB], (unsigned long long)tw[1]);
+                atomicAdd(&a.counters[4 + kTMmaWaitAcc], (unsigned long long)tw[2]);
             }
         }
         __syncwarp();
@@ -435,6 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
         int* qcount = reinterpret_cast<int*>(sm + P.qcount);
         int g = 0;
         bool ok = true;
+        long long te[4] = {0, 0, 0, 0};
         for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
             if (!mbar_wait(a_full, t & 1, abort_flag, a.err, 6)) { ok = false; break; }
             const float Ui = reinterpret_cast<const float*>(sm + P.arow_u)[ra];
@@ -442,7 +470,10 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
             const int nu = item_units(a, item, p_lo);
             for (int uix = 0; uix < nu; ++uix, ++g) {
                 const int s = g & 1, qi = g % 3;
+                long long c0 = clock64();
                 if (!mbar_wait(&acc_full[s], (g >> 1) & 1, abort_flag, a.err, 7)) { ok = false; break; }
+                long long c1 = clock64();
+                te[0] += c1 - c0;
                 tc_fence_after();
                 const Unit u = make_unit(a, item, p_lo + uix);
                 const int gi = u.B * kRows + ra;
@@ -563,8 +594,12 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                     qcount[4 + (g + 1) % 3] = kQueueCap;
                 }
                 __syncwarp();
+                long long c2 = clock64();
+                te[1] += c2 - c1;
                 if (lane == 0) mbar_arrive(epi_bar);
                 if (!mbar_wait(epi_bar, g & 1, abort_flag, a.err, 8)) { ok = false; break; }
+                long long c3 = clock64();
+                te[2] += c3 - c2;
                 // ---- phase 2: refine the queued pairs, all lanes busy
                 const int nq = min(qcount[qi], qcount[4 + qi]);
                 for (int ei = e * 32 + lane; ei < nq; ei += 256) {
@@ -588,10 +623,17 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
+                te[3] += clock64() - c3;
                 if (lane == 0) mbar_arrive(&b_empty[s]);
             }
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(a_empty);
+        }
+        if (a.counters && lane == 0) {
+            atomicAdd(&a.counters[4 + kTEpiWaitAcc], (unsigned long long)te[0]);
+            atomicAdd(&a.counters[4 + kTEpiP1], (unsigned long long)te[1]);
+            atomicAdd(&a.counters[4 + kTEpiBar], (unsigned long long)te[2]);
+            atomicAdd(&a.counters[4 + kTEpiP2], (unsigned long long)te[3]);
         }
     }
 
