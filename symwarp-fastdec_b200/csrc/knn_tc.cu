@@ -157,9 +157,10 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar)
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
+// tcgen05.ld of 32 consecutive accumulator columns of this thread's TMEM lane; the registers are
+// valid only after tmem_wait on the same array (the wait names them, so no use moves above it)
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
 {
-    uint32_t r[32];
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -169,9 +170,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int t = 0; t < 32; ++t) v[t] = __uint_as_float(r[t]);
+}
+
+__device__ __forceinline__ void tmem_wait(uint32_t (&r)[32])
+{
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
 }
 
 // ------------------------------------------------------------------ shared memory plan
@@ -485,36 +495,28 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                 float* qa = qacc + qi * kQueueCap;
                 const int rblk = half ? u.R1 : u.R0;
                 // ---- phase 1: filter the accumulator, queue the survivors
-                for (int c = 0; c < 4 && rblk >= 0; ++c) {
+                auto process = [&](const uint32_t (&rv)[32], int c) {
                     const int cb = half * 128 + c * 32;
-                    float v[32];
-                    tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(s * kCols + cb), v);
-                    float uc[32];
+                    bool rh = false, ch = false;
 #pragma unroll
                     for (int q = 0; q < 32; q += 4) {
                         const float4 u4 = *reinterpret_cast<const float4*>(cu + cb + q);
-                        uc[q] = u4.x;
-                        uc[q + 1] = u4.y;
-                        uc[q + 2] = u4.z;
-                        uc[q + 3] = u4.w;
-                    }
-                    bool rh = false, ch = false;
-#pragma unroll
-                    for (int q = 0; q < 32; ++q) {
-                        rh = rh || (v[q] <= Ui);
-                        ch = ch || (v[q] <= uc[q]);
+                        const float v0 = __uint_as_float(rv[q]), v1 = __uint_as_float(rv[q + 1]);
+                        const float v2 = __uint_as_float(rv[q + 2]), v3 = __uint_as_float(rv[q + 3]);
+                        rh |= (v0 <= Ui) | (v1 <= Ui) | (v2 <= Ui) | (v3 <= Ui);
+                        ch |= (v0 <= u4.x) | (v1 <= u4.y) | (v2 <= u4.z) | (v3 <= u4.w);
                     }
                     rh = rh && row_real;
                     ch = ch && row_real && !a.diag;   // diagonal units: both orders are rows
-                    if (!__any_sync(0xffffffffu, rh || ch)) continue;
+                    if (!__any_sync(0xffffffffu, rh || ch)) return;
                     unsigned mrow = 0, mcol = 0;
                     if (rh) {
 #pragma unroll
-                        for (int q = 0; q < 32; ++q) mrow |= (v[q] <= Ui ? 1u : 0u) << q;
+                        for (int q = 0; q < 32; ++q) mrow |= (__uint_as_float(rv[q]) <= Ui ? 1u : 0u) << q;
                     }
                     if (ch) {
 #pragma unroll
-                        for (int q = 0; q < 32; ++q) mcol |= (v[q] <= uc[q] ? 1u : 0u) << q;
+                        for (int q = 0; q < 32; ++q) mcol |= (__uint_as_float(rv[q]) <= cu[cb + q] ? 1u : 0u) << q;
                     }
                     unsigned m = mrow | mcol;
                     const int mine = __popc(m);
@@ -534,29 +536,29 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                     }
                     if (base + total <= kQueueCap) {
                         int pos = base + incl - mine;
+                        const int p0 = pos;
                         while (m) {
                             const int q = __ffs(m) - 1;
                             m &= m - 1;
                             const unsigned bit = 1u << q;
-                            queue[pos] = (uint32_t)ra | ((uint32_t)(cb + q) << 8) | ((mrow & bit) ? 1u << 16 : 0u) |
-                                         ((mcol & bit) ? 1u << 17 : 0u);
-                            ++pos;
+                            queue[pos++] = (uint32_t)ra | ((uint32_t)(cb + q) << 8) | ((mrow & bit) ? 1u << 16 : 0u) |
+                                           ((mcol & bit) ? 1u << 17 : 0u);
                         }
                         if (!a.exact) {
                             // TF32 mode keeps acc itself: store it with a static index
-                            int p2 = base + incl - mine;
+                            int p2 = p0;
 #pragma unroll
                             for (int q = 0; q < 32; ++q)
-                                if ((mrow | mcol) & (1u << q)) qa[p2++] = v[q];
+                                if ((mrow | mcol) & (1u << q)) qa[p2++] = __uint_as_float(rv[q]);
                         }
                     } else {
                         // queue full (early rounds): reservations are granted in order, so entries are
                         // valid up to the first failed one; this chunk drains in place instead
                         if (lane == 0) atomicMin(&qcount[4 + qi], base);
+                        float* scr = qacc + 3 * kQueueCap + e * 32 * 33;
                         if (!a.exact) {
-                            float* scr = qacc + 3 * kQueueCap + e * 32 * 33;
 #pragma unroll
-                            for (int q = 0; q < 32; ++q) scr[lane * 33 + q] = v[q];
+                            for (int q = 0; q < 32; ++q) scr[lane * 33 + q] = __uint_as_float(rv[q]);
                         }
                         while (__any_sync(0xffffffffu, m != 0u)) {
                             if (m) {
@@ -568,7 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                                 if (gj != gi && gj < a.n) {
                                     const float d2 = a.exact
                                         ? refine_d2(sm + P.a, am, ra, bb, bm, jloc, a.d, a.dm, a.nrm[gi], a.nrm[gj])
-                                        : fmaxf(qacc[3 * kQueueCap + e * 32 * 33 + lane * 33 + q], 0.0f);
+                                        : fmaxf(scr[lane * 33 + q], 0.0f);
                                     if (mrow & bit) {
                                         const uint64_t key = pack_key(d2, gj);
                                         if (key < a.thr[gi]) tc_append(a, gi, key);
@@ -582,6 +584,23 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                         }
                     }
                     __syncwarp();
+                };
+                if (rblk >= 0) {
+                    // two chunks in flight: the TMEM load of chunk c + 1 overlaps the filter of chunk c
+                    const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(s * kCols + half * 128);
+                    uint32_t ra0[32], ra1[32];
+                    tmem_ld32(tbase, ra0);
+                    tmem_wait(ra0);
+                    tmem_ld32(tbase + 32, ra1);
+                    process(ra0, 0);
+                    tmem_wait(ra1);
+                    tmem_ld32(tbase + 64, ra0);
+                    process(ra1, 1);
+                    tmem_wait(ra0);
+                    tmem_ld32(tbase + 96, ra1);
+                    process(ra0, 2);
+                    tmem_wait(ra1);
+                    process(ra1, 3);
                 }
                 // the accumulator is no longer needed: let the MMA of a later tile reuse it
                 tc_fence_before();
