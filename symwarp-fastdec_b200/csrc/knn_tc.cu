@@ -80,15 +80,17 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* b)
 {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
 }
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes (or ~1 ms
+// passes) instead of spinning, so waiting roles do not take issue slots from the epilogue
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity)
 {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(su32(b)), "r"(parity)
+        : "r"(su32(b)), "r"(parity), "r"(1000000u)
         : "memory");
     return ok != 0;
 }
