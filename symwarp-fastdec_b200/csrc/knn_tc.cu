@@ -187,7 +187,7 @@ __device__ __forceinline__ void tmem_wait(uint32_t (&r)[32])
 }
 
 // ------------------------------------------------------------------ shared memory plan
-constexpr int kQueueCap = 1024;          // survivor entries per tile queue (three queues)
+constexpr int kQueueCap = 256;           // (row, chunk, masks) entries per tile queue (three queues)
 
 struct Smem {
     // offsets in bytes from the 1024-aligned base
@@ -212,8 +212,8 @@ __host__ __device__ inline Smem smem_plan(int kp, int dm)
     o += (uint32_t)kCols * dm * 2;
     s.bm1 = o;
     o += (uint32_t)kCols * dm * 2;
-    // TF32 mode: queued acc values plus the in-place drain stash of every epilogue warp
-    const uint32_t accq = 3u * kQueueCap * 4u + kEpiWarps * 32 * 33 * 4;
+    // TF32 mode: the in-place drain stash of every epilogue warp
+    const uint32_t accq = kEpiWarps * 32 * 33 * 4;
     if (o - s.am < accq) o = s.am + accq;
     o = (o + 15) & ~15u;
     s.arow_u = o;
@@ -222,8 +222,8 @@ __host__ __device__ inline Smem smem_plan(int kp, int dm)
         s.bcol_u[q] = o;
         o += kCols * 4;
     }
-    s.queue = o;
-    o += 3u * kQueueCap * 4u;
+    s.queue = o;                       // per queue: meta[cap], row masks[cap], column masks[cap]
+    o += 3u * kQueueCap * 12u;
     s.qcount = o;                      // [0..2] reserved entries, [4..6] end of the written prefix
     o += 32;
     s.bars = o;
@@ -349,7 +349,6 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
         mbar_init(epi_bar, kEpiWarps);
         int* qc = reinterpret_cast<int*>(sm + P.qcount);
         qc[0] = qc[1] = qc[2] = 0;
-        qc[4] = qc[5] = qc[6] = kQueueCap;
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -470,7 +469,6 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
         const int ra = quad * 32 + lane;        // this thread's A row (tile-local)
         const int16_t* am = reinterpret_cast<const int16_t*>(sm + P.am);
         uint32_t* queues = reinterpret_cast<uint32_t*>(sm + P.queue);
-        float* qacc = reinterpret_cast<float*>(sm + P.am);          // TF32 mode: acc of queued pairs
         int* qcount = reinterpret_cast<int*>(sm + P.qcount);
         int g = 0;
         bool ok = true;
@@ -493,95 +491,63 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                 const unsigned char* bb = sm + (s ? P.b1 : P.b0);
                 const int16_t* bm = reinterpret_cast<const int16_t*>(sm + (s ? P.bm1 : P.bm0));
                 const float* cu = reinterpret_cast<const float*>(sm + P.bcol_u[s]);
-                uint32_t* queue = queues + qi * kQueueCap;
-                float* qa = qacc + qi * kQueueCap;
+                uint32_t* qmeta = queues + qi * 3 * kQueueCap;
+                uint32_t* qrow = qmeta + kQueueCap;
+                uint32_t* qcol = qrow + kQueueCap;
                 const int rblk = half ? u.R1 : u.R0;
                 // ---- phase 1: filter the accumulator, queue the survivors
+                // one pair's survivors, handled in place (queue full, or TF32 mode where acc is the d2)
+                auto settle = [&](int c, int q, bool row_hit, bool col_hit, float accv) {
+                    const int jloc = half * 128 + c * 32 + q;
+                    const int gj = rblk * kRows + c * 32 + q;
+                    if (gj == gi || gj >= a.n) return;
+                    const float d2 = a.exact ? refine_d2(sm + P.a, am, ra, bb, bm, jloc, a.d, a.dm, a.nrm[gi], a.nrm[gj])
+                                             : fmaxf(accv, 0.0f);
+                    if (row_hit) {
+                        const uint64_t key = pack_key(d2, gj);
+                        if (key < a.thr[gi]) tc_append(a, gi, key);
+                    }
+                    if (col_hit) {
+                        const uint64_t key = pack_key(d2, gi);
+                        if (key < a.thr[gj]) tc_append(a, gj, key);
+                    }
+                };
                 auto process = [&](const uint32_t (&rv)[32], int c) {
                     const int cb = half * 128 + c * 32;
-                    bool rh = false, ch = false;
+                    unsigned mrow = 0, mcol = 0;
 #pragma unroll
                     for (int q = 0; q < 32; q += 4) {
                         const float4 u4 = *reinterpret_cast<const float4*>(cu + cb + q);
-                        const float v0 = __uint_as_float(rv[q]), v1 = __uint_as_float(rv[q + 1]);
-                        const float v2 = __uint_as_float(rv[q + 2]), v3 = __uint_as_float(rv[q + 3]);
-                        rh |= (v0 <= Ui) | (v1 <= Ui) | (v2 <= Ui) | (v3 <= Ui);
-                        ch |= (v0 <= u4.x) | (v1 <= u4.y) | (v2 <= u4.z) | (v3 <= u4.w);
-                    }
-                    rh = rh && row_real;
-                    ch = ch && row_real && !a.diag;   // diagonal units: both orders are rows
-                    if (!__any_sync(0xffffffffu, rh || ch)) return;
-                    unsigned mrow = 0, mcol = 0;
-                    if (rh) {
+                        const float uc[4] = {u4.x, u4.y, u4.z, u4.w};
 #pragma unroll
-                        for (int q = 0; q < 32; ++q) mrow |= (__uint_as_float(rv[q]) <= Ui ? 1u : 0u) << q;
-                    }
-                    if (ch) {
-#pragma unroll
-                        for (int q = 0; q < 32; ++q) mcol |= (__uint_as_float(rv[q]) <= cu[cb + q] ? 1u : 0u) << q;
-                    }
-                    unsigned m = mrow | mcol;
-                    const int mine = __popc(m);
-                    int incl = mine;
-#pragma unroll
-                    for (int off = 1; off < 32; off <<= 1) {
-                        const int o = __shfl_up_sync(0xffffffffu, incl, off);
-                        if (lane >= off) incl += o;
-                    }
-                    const int total = __shfl_sync(0xffffffffu, incl, 31);
-                    int base = 0;
-                    if (lane == 0) base = atomicAdd(&qcount[qi], total);
-                    base = __shfl_sync(0xffffffffu, base, 0);
-                    if (a.counters && lane == 0) {
-                        atomicAdd(&a.counters[0], (unsigned long long)total);
-                        atomicAdd(&a.counters[1], 1ull);
-                    }
-                    if (base + total <= kQueueCap) {
-                        int pos = base + incl - mine;
-                        const int p0 = pos;
-                        while (m) {
-                            const int q = __ffs(m) - 1;
-                            m &= m - 1;
-                            const unsigned bit = 1u << q;
-                            queue[pos++] = (uint32_t)ra | ((uint32_t)(cb + q) << 8) | ((mrow & bit) ? 1u << 16 : 0u) |
-                                           ((mcol & bit) ? 1u << 17 : 0u);
+                        for (int w = 0; w < 4; ++w) {
+                            const float v = __uint_as_float(rv[q + w]);
+                            if (v <= Ui) mrow |= 1u << (q + w);
+                            if (v <= uc[w]) mcol |= 1u << (q + w);
                         }
-                        if (!a.exact) {
-                            // TF32 mode keeps acc itself: store it with a static index
-                            int p2 = p0;
+                    }
+                    if (!row_real) mrow = 0;
+                    if (!row_real || a.diag) mcol = 0;   // diagonal units: both orders are rows
+                    const unsigned m = mrow | mcol;
+                    if (!__any_sync(0xffffffffu, m != 0u)) return;
+                    if (!a.exact) {
+                        float* scr = reinterpret_cast<float*>(sm + P.am) + e * 32 * 33;
 #pragma unroll
-                            for (int q = 0; q < 32; ++q)
-                                if ((mrow | mcol) & (1u << q)) qa[p2++] = __uint_as_float(rv[q]);
+                        for (int q = 0; q < 32; ++q) scr[lane * 33 + q] = __uint_as_float(rv[q]);
+                        for (unsigned mm = m; mm; mm &= mm - 1) {
+                            const int q = __ffs(mm) - 1;
+                            settle(c, q, (mrow >> q) & 1u, (mcol >> q) & 1u, scr[lane * 33 + q]);
                         }
-                    } else {
-                        // queue full (early rounds): reservations are granted in order, so entries are
-                        // valid up to the first failed one; this chunk drains in place instead
-                        if (lane == 0) atomicMin(&qcount[4 + qi], base);
-                        float* scr = qacc + 3 * kQueueCap + e * 32 * 33;
-                        if (!a.exact) {
-#pragma unroll
-                            for (int q = 0; q < 32; ++q) scr[lane * 33 + q] = __uint_as_float(rv[q]);
-                        }
-                        while (__any_sync(0xffffffffu, m != 0u)) {
-                            if (m) {
-                                const int q = __ffs(m) - 1;
-                                m &= m - 1;
-                                const unsigned bit = 1u << q;
-                                const int jloc = cb + q;
-                                const int gj = rblk * kRows + c * 32 + q;
-                                if (gj != gi && gj < a.n) {
-                                    const float d2 = a.exact
-                                        ? refine_d2(sm + P.a, am, ra, bb, bm, jloc, a.d, a.dm, a.nrm[gi], a.nrm[gj])
-                                        : fmaxf(scr[lane * 33 + q], 0.0f);
-                                    if (mrow & bit) {
-                                        const uint64_t key = pack_key(d2, gj);
-                                        if (key < a.thr[gi]) tc_append(a, gi, key);
-                                    }
-                                    if (mcol & bit) {
-                                        const uint64_t key = pack_key(d2, gi);
-                                        if (key < a.thr[gj]) tc_append(a, gj, key);
-                                    }
-                                }
+                    } else if (m) {
+                        const int slot = atomicAdd(&qcount[qi], 1);
+                        if (slot < kQueueCap) {
+                            qmeta[slot] = (uint32_t)ra | ((uint32_t)c << 8) | ((uint32_t)half << 10);
+                            qrow[slot] = mrow;
+                            qcol[slot] = mcol;
+                        } else {
+                            for (unsigned mm = m; mm; mm &= mm - 1) {
+                                const int q = __ffs(mm) - 1;
+                                settle(c, q, (mrow >> q) & 1u, (mcol >> q) & 1u, 0.0f);
                             }
                         }
                     }
@@ -610,10 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                 if (lane == 0) mbar_arrive(&acc_empty[s]);
                 // queue (g + 1) % 3 last served tile g - 2, which every warp finished before the
                 // previous barrier; reset it before this barrier so tile g + 1 starts empty
-                if (e == 0 && lane == 0) {
-                    qcount[(g + 1) % 3] = 0;
-                    qcount[4 + (g + 1) % 3] = kQueueCap;
-                }
+                if (e == 0 && lane == 0) qcount[(g + 1) % 3] = 0;
                 __syncwarp();
                 long long c2 = clock64();
                 te[1] += c2 - c1;
@@ -621,25 +584,31 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                 if (!mbar_wait(epi_bar, g & 1, abort_flag, a.err, 8)) { ok = false; break; }
                 long long c3 = clock64();
                 te[2] += c3 - c2;
-                // ---- phase 2: refine the queued pairs, all lanes busy
-                const int nq = min(qcount[qi], qcount[4 + qi]);
-                for (int ei = e * 32 + lane; ei < nq; ei += 256) {
-                    const uint32_t ent = queue[ei];
-                    const int qa_row = ent & 0xFF, jloc = (ent >> 8) & 0xFF;
-                    const int gi2 = u.B * kRows + qa_row;
-                    const int rb2 = (jloc < kRows) ? u.R0 : u.R1;
-                    const int gj = rb2 * kRows + (jloc & (kRows - 1));
-                    if (gj == gi2 || gj >= a.n) continue;
-                    const float d2 = a.exact
-                        ? refine_d2(sm + P.a, am, qa_row, bb, bm, jloc, a.d, a.dm, a.nrm[gi2], a.nrm[gj])
-                        : fmaxf(qacc[qi * kQueueCap + ei], 0.0f);
-                    if (ent & (1u << 16)) {
-                        const uint64_t key = pack_key(d2, gj);
-                        if (key < a.thr[gi2]) tc_append(a, gi2, key);
-                    }
-                    if (ent & (1u << 17)) {
-                        const uint64_t key = pack_key(d2, gi2);
-                        if (key < a.thr[gj]) tc_append(a, gj, key);
+                // ---- phase 2: refine the queued survivors; entries are dealt round-robin to the warps
+                const int nq = min(qcount[qi], kQueueCap);
+                for (int ei = lane * kEpiWarps + e; ei < nq; ei += 32 * kEpiWarps) {
+                    const uint32_t meta = qmeta[ei];
+                    const int qrw = meta & 0xFF, c = (meta >> 8) & 3;
+                    const unsigned mr = qrow[ei], mc = qcol[ei];
+                    const int gi2 = u.B * kRows + qrw;
+                    // this entry's chunk and half follow from the warp that queued it: c is the chunk,
+                    // the half is stored in bit 10
+                    const int hf = (meta >> 10) & 1;
+                    const int rb2 = hf ? u.R1 : u.R0;
+                    for (unsigned mm = mr | mc; mm; mm &= mm - 1) {
+                        const int q = __ffs(mm) - 1;
+                        const int jloc = hf * 128 + c * 32 + q;
+                        const int gj = rb2 * kRows + c * 32 + q;
+                        if (gj == gi2 || gj >= a.n) continue;
+                        const float d2 = refine_d2(sm + P.a, am, qrw, bb, bm, jloc, a.d, a.dm, a.nrm[gi2], a.nrm[gj]);
+                        if ((mr >> q) & 1u) {
+                            const uint64_t key = pack_key(d2, gj);
+                            if (key < a.thr[gi2]) tc_append(a, gi2, key);
+                        }
+                        if ((mc >> q) & 1u) {
+                            const uint64_t key = pack_key(d2, gi2);
+                            if (key < a.thr[gj]) tc_append(a, gj, key);
+                        }
                     }
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
