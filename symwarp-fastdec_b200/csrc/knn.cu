@@ -474,11 +474,12 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
             if (engine == FDB200_ENGINE_TCGEN05 && !r.diag) {
                 // per tcgen05 tile (= two offsets), cycles per CTA role instance
                 const double tiles = (double)units / 2.0;
-                const double per_ep = tiles * 8.0;   // epilogue warp-tiles
+                const double per_f = tiles * 8.0;   // filter warp-tiles (each tile has one refine warp)
                 fprintf(stderr, "[fdb200]   cycles/tile: prod wait A %.0f B %.0f | mma wait A %.0f B %.0f acc %.0f |"
-                                " epi wait acc %.0f filter %.0f bar %.0f refine %.0f\n",
-                        cn[4] / tiles, cn[5] / tiles, cn[6] / tiles, cn[7] / tiles, cn[8] / tiles, cn[9] / per_ep,
-                        cn[10] / per_ep, cn[11] / per_ep, cn[12] / per_ep);
+                                " filter wait %.0f work %.0f | refine wait %.0f work %.0f | entries/tile %.1f"
+                                " inline %llu\n",
+                        cn[4] / tiles, cn[5] / tiles, cn[6] / tiles, cn[7] / tiles, cn[8] / tiles, cn[9] / per_f,
+                        cn[10] / per_f, cn[11] / tiles, cn[12] / tiles, cn[0] / tiles, cn[1]);
             }
         }
         if (!diag_done) {

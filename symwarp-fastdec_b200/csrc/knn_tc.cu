@@ -4,7 +4,7 @@
 // lexicographic admission, see knn.cu); only the way candidates are found differs:
 //
 //   1. TF32 filter on the tensor cores. Every coordinate is rounded to TF32 (nearest) once,
-//      x~ = rna(x), and each point is stored twice, point-major, K = D + 6 padded to 8:
+//      x~ = rna(x), and each point is stored twice, K = D + 6 padded to 8:
 //          A row i = [-2 x~_i, 1, 1, 1, nh_i, nm_i, nl_i, 0...]
 //          B row j = [x~_j, nh_j, nm_j, nl_j, 1, 1, 1, 0...]
 //      with nh + nm + nl = |x~|^2 (fmaf chain) split into three TF32-exact parts. Every operand is
@@ -13,24 +13,25 @@
 //   2. Rigorous margin (filter_bound in knn_common.cuh): a candidate that can still enter point
 //      i's list always has acc <= U_i, so filtering on acc <= U never changes the result.
 //   3. Exact refine. A pair passing acc <= U_row or acc <= U_col is recomputed with the sequential
-//      fmaf chain on the ORIGINAL coordinates, rebuilt bit-exactly in shared memory from x~ and
-//      the int16 residual m = bits(x) - bits(x~) (|m| <= 2^12), then admitted with the exact
-//      lexicographic test. Precision TF32 skips the refine and keeps d2 = max(acc, 0).
+//      fmaf chain on the ORIGINAL FP32 coordinates (a point-major copy in global memory) and
+//      admitted with the exact lexicographic test. Precision TF32 skips the refine and keeps
+//      d2 = max(acc, 0).
 //
-// Kernel shape (persistent, one CTA per SM, 320 threads):
-//   warp 0      producer: bulk copies (cp.async.bulk) of the A tile (128 rows, resident for a work
-//               item) and double-buffered B tiles (two 128-point blocks = 256 rows), stored in
-//               global memory as pre-swizzled 4 KB K panels (the SWIZZLE_32B K-major layout), plus
-//               residual rows and filter bounds
-//   warp 1      TMEM owner and MMA issuer (one thread): K/8 tcgen05.mma kind::tf32 per tile into
-//               one of two 256-column TMEM accumulators, tcgen05.commit to an mbarrier
-//   warps 2..9  epilogue: tcgen05.ld 32 columns at a time, OR-accumulated two-sided filter; on a
-//               hit, per-lane survivor masks drained one column per lane per step (refine +
-//               append); then release the accumulator and the B stage
+// Kernel shape (persistent, one CTA per SM, 13 warps):
+//   warp 0       producer: cp.async.bulk copies of the A tile (128 rows, resident for a work item)
+//                and of three B stages (two 128-point blocks = 256 rows each), stored in global
+//                memory as pre-swizzled 4 KB K panels (the SWIZZLE_32B K-major layout), plus the
+//                filter bounds of the tile's rows and columns
+//   warp 1       TMEM owner and MMA issuer (one thread): K/8 tcgen05.mma kind::tf32 per tile into
+//                one of two 256-column TMEM accumulators, tcgen05.commit to an mbarrier
+//   warps 2..9   filter: tcgen05.ld 32 columns at a time (two loads in flight), two-sided bound
+//                test into per-row survivor masks, one queue entry per (row, 32 columns) with
+//                survivors; then the accumulator and the B stage are released at once
+//   warps 10..12 refine: warp r owns the tiles g = r mod 3 and drains their queues (exact refine
+//                from global memory, admission, append), off the filter's critical path
 // Every mbarrier wait is bounded (about a second); on a timeout the CTA records an error code,
 // stops issuing work, frees its TMEM and returns, and the host reports the failure.
 #include "knn_common.cuh"
-
 
 #include <algorithm>
 #include <cmath>
@@ -40,29 +41,33 @@ namespace fdb {
 
 namespace tc {
 
-constexpr int kThreads = 320;
-constexpr int kEpiWarps = 8;
+constexpr int kFilterWarps = 8;
+constexpr int kRefineWarps = 3;
+constexpr int kThreads = 32 * (2 + kFilterWarps + kRefineWarps);
 constexpr int kRows = 128;               // A rows per tile
 constexpr int kCols = 256;               // B rows per tile (two blocks)
-constexpr int kMaxKp = 72;               // K up to 72 floats (nine 32-byte panels)
+constexpr int kStages = 3;               // B stages in shared memory
+constexpr int kQueues = 4;               // survivor queues between filter and refine warps
+constexpr int kQueueCap = 256;           // entries per queue
+constexpr int kMaxKp = 64;               // K up to 64 floats (eight 32-byte panels)
 constexpr long long kWaitCycles = 2000000000ll;   // ~1 s at 2 GHz
 constexpr float kPoisonNorm = 1.2676506002282294e30f;   // 2^100, exact in TF32
 
 struct Args {
-    int n, d, kp, dm, T, b_lo, nb, cap, exact;
+    int n, d, kp, dp, T, b_lo, nb, cap, exact;
     int diag, delta0, ndelta, npairs, pairs_per_item, items;
     int row_pad;                 // Npad: first poison row of the B array
     const float* U;              // filter bounds (Npad + 128)
     const float* nrm;            // exact fp32 norms (Npad + 128)
     const uint64_t* thr;         // exact admission thresholds (Npad + 128)
-    const int16_t* resid;        // bits(x) - bits(x~), dm per row (Npad + 128 rows)
+    const float* xp;             // original coordinates, point-major, dp floats per row
     const unsigned char* aimg;   // A operand: per 128-row block, K/8 pre-swizzled 4 KB panels
     const unsigned char* bimg;   // B operand, same layout (Npad + 128 rows)
     uint64_t* cand;
     int* cnt;
     int* ovf;
     int* err;
-    unsigned long long* counters;   // [0] refined pairs, [1] chunks with survivors, [2] drain steps
+    unsigned long long* counters;   // optional trace counters
 };
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -81,7 +86,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* b)
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
 }
 // try_wait with a suspend-time hint: the thread sleeps until the phase completes (or ~1 ms
-// passes) instead of spinning, so waiting roles do not take issue slots from the epilogue
+// passes) instead of spinning, so waiting roles do not take issue slots from the filter
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity)
 {
     uint32_t ok;
@@ -97,7 +102,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity)
 
 // trace-mode phase timers: cycles accumulated per role, added to counters[4 + slot] at the end
 enum {
-    kTProdWaitA, kTProdWaitB, kTMmaWaitA, kTMmaWaitB, kTMmaWaitAcc, kTEpiWaitAcc, kTEpiP1, kTEpiBar, kTEpiP2,
+    kTProdWaitA, kTProdWaitB, kTMmaWaitA, kTMmaWaitB, kTMmaWaitAcc, kTFiltWait, kTFiltWork, kTRefWait, kTRefWork,
     kTNum
 };
 
@@ -187,87 +192,38 @@ __device__ __forceinline__ void tmem_wait(uint32_t (&r)[32])
 }
 
 // ------------------------------------------------------------------ shared memory plan
-constexpr int kQueueCap = 256;           // (row, chunk, masks) entries per tile queue (three queues)
-
 struct Smem {
     // offsets in bytes from the 1024-aligned base
-    uint32_t a, b0, b1, am, bm0, bm1, arow_u, bcol_u[2], queue, qcount, bars, misc, total;
+    uint32_t a, b[kStages], arow_u, bcol_u[kStages], queue, qcount, bars, misc, total;
 };
 
-// dm: residual entries per row (D rounded up to 8, so a 128-row block is a 16-byte multiple)
-__host__ __device__ inline Smem smem_plan(int kp, int dm)
+__host__ __device__ inline Smem smem_plan(int kp)
 {
     Smem s;
     const uint32_t panels = (uint32_t)kp / 8;
     uint32_t o = 0;
     s.a = o;
     o += panels * kRows * 32;
-    s.b0 = o;
-    o += panels * kCols * 32;
-    s.b1 = o;
-    o += panels * kCols * 32;
-    s.am = o;                          // residuals of the A tile (exact mode) or queued acc (TF32 mode)
-    o += (uint32_t)kRows * dm * 2;
-    s.bm0 = o;
-    o += (uint32_t)kCols * dm * 2;
-    s.bm1 = o;
-    o += (uint32_t)kCols * dm * 2;
-    // TF32 mode: the in-place drain stash of every epilogue warp
-    const uint32_t accq = kEpiWarps * 32 * 33 * 4;
-    if (o - s.am < accq) o = s.am + accq;
-    o = (o + 15) & ~15u;
+    for (int q = 0; q < kStages; ++q) {
+        s.b[q] = o;
+        o += panels * kCols * 32;
+    }
     s.arow_u = o;
     o += kRows * 4;
-    for (int q = 0; q < 2; ++q) {
+    for (int q = 0; q < kStages; ++q) {
         s.bcol_u[q] = o;
         o += kCols * 4;
     }
-    s.queue = o;                       // per queue: meta[cap], row masks[cap], column masks[cap]
-    o += 3u * kQueueCap * 12u;
-    s.qcount = o;                      // [0..2] reserved entries, [4..6] end of the written prefix
-    o += 32;
+    s.queue = o;                       // per queue: rows[cap], first columns[cap], row masks, column masks
+    o += (uint32_t)kQueues * kQueueCap * 16u;
+    s.qcount = o;
+    o += 16 * 4;
     s.bars = o;
-    o += 16 * 8;
+    o += 24 * 8;
     s.misc = o;
     o += 64;
     s.total = o;
     return s;
-}
-
-// element (row, k) of a K-major SW32 panel set: panel k/8, 16-byte chunk swizzled by row bit 2
-__device__ __forceinline__ const float4* panel_chunk(const unsigned char* base, int rows_per_panel, int row,
-                                                     int chunk)
-{
-    const int panel = chunk >> 1, half = chunk & 1;
-    const int phys = half ^ ((row >> 2) & 1);
-    return reinterpret_cast<const float4*>(base + (size_t)panel * rows_per_panel * 32 + row * 32 + phys * 16);
-}
-
-// original coordinate from its TF32 rounding and the stored bit difference
-__device__ __forceinline__ float rebuild(float xt, int16_t m) { return __int_as_float(__float_as_int(xt) + (int)m); }
-
-// exact d2 of (A row ra, B row rb): fmaf chain over d = 0..D-1 on the rebuilt FP32 coordinates
-__device__ __forceinline__ float refine_d2(const unsigned char* abase, const int16_t* am, int ra,
-                                           const unsigned char* bbase, const int16_t* bm, int rb, int d, int dm,
-                                           float na, float nb)
-{
-    float dot = 0.0f;
-    const int chunks = (d + 3) >> 2;
-    const int16_t* ar = am + (size_t)ra * dm;
-    const int16_t* br = bm + (size_t)rb * dm;
-    for (int c = 0; c < chunks; ++c) {
-        const float4 av = *panel_chunk(abase, kRows, ra, c);
-        const float4 bv = *panel_chunk(bbase, kCols, rb, c);
-        const short4 ma = *reinterpret_cast<const short4*>(ar + 4 * c);
-        const short4 mb = *reinterpret_cast<const short4*>(br + 4 * c);
-        const float xa[4] = {rebuild(__fmul_rn(-0.5f, av.x), ma.x), rebuild(__fmul_rn(-0.5f, av.y), ma.y),
-                             rebuild(__fmul_rn(-0.5f, av.z), ma.z), rebuild(__fmul_rn(-0.5f, av.w), ma.w)};
-        const float xb[4] = {rebuild(bv.x, mb.x), rebuild(bv.y, mb.y), rebuild(bv.z, mb.z), rebuild(bv.w, mb.w)};
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-            if (c * 4 + e < d) dot = __fmaf_rn(xa[e], xb[e], dot);
-    }
-    return exact_d2(na, nb, dot);
 }
 
 // unit (item, index inside item) -> Q block and the two R blocks (-1 = poison half)
@@ -319,36 +275,83 @@ __device__ __forceinline__ void tc_append(const Args& a, int p, uint64_t key)
     else atomicOr(a.ovf, 1);
 }
 
+// exact d2 of two points from the point-major original coordinates: fmaf chain over d = 0..D-1
+// (the zero padding is never fed to the chain: fmaf(0, 0, -0) would turn a -0 dot into +0)
+__device__ __forceinline__ float refine_global(const Args& a, int gi, int gj)
+{
+    const float* xi = a.xp + (size_t)gi * a.dp;
+    const float* xj = a.xp + (size_t)gj * a.dp;
+    const float4* xi4 = reinterpret_cast<const float4*>(xi);
+    const float4* xj4 = reinterpret_cast<const float4*>(xj);
+    float dot = 0.0f;
+    const int full = a.d >> 2;
+    for (int c = 0; c < full; ++c) {
+        const float4 u = __ldg(xi4 + c), v = __ldg(xj4 + c);
+        dot = __fmaf_rn(u.x, v.x, dot);
+        dot = __fmaf_rn(u.y, v.y, dot);
+        dot = __fmaf_rn(u.z, v.z, dot);
+        dot = __fmaf_rn(u.w, v.w, dot);
+    }
+    for (int k = full * 4; k < a.d; ++k) dot = __fmaf_rn(__ldg(xi + k), __ldg(xj + k), dot);
+    return exact_d2(__ldg(a.nrm + gi), __ldg(a.nrm + gj), dot);
+}
+
+// the survivors of one (row gi, 32 columns from gj0): exact refine and admission on both sides
+__device__ __forceinline__ void settle_exact(const Args& a, int gi, int gj0, unsigned mr, unsigned mc)
+{
+    for (unsigned mm = mr | mc; mm; mm &= mm - 1) {
+        const int q = __ffs(mm) - 1;
+        const int gj = gj0 + q;
+        if (gj == gi || gj >= a.n) continue;
+        const float d2 = refine_global(a, gi, gj);
+        if ((mr >> q) & 1u) {
+            const uint64_t key = pack_key(d2, gj);
+            if (key < __ldg(a.thr + gi)) tc_append(a, gi, key);
+        }
+        if ((mc >> q) & 1u) {
+            const uint64_t key = pack_key(d2, gi);
+            if (key < __ldg(a.thr + gj)) tc_append(a, gj, key);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    const Smem P = smem_plan(a.kp, a.dm);
+    const Smem P = smem_plan(a.kp);
     const int panels = a.kp / 8;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P.bars);
     uint64_t* a_full = bars + 0;
     uint64_t* a_empty = bars + 1;
-    uint64_t* b_full = bars + 2;      // [2]
-    uint64_t* b_empty = bars + 4;     // [2]
-    uint64_t* acc_full = bars + 6;    // [2]
-    uint64_t* acc_empty = bars + 8;   // [2]
-    uint64_t* epi_bar = bars + 10;    // the 8 epilogue warps, once per tile
+    uint64_t* b_full = bars + 2;                     // [kStages]
+    uint64_t* b_empty = b_full + kStages;            // [kStages]
+    uint64_t* acc_full = b_empty + kStages;          // [2]
+    uint64_t* acc_empty = acc_full + 2;              // [2]
+    uint64_t* q_full = acc_empty + 2;                // [kQueues]
+    uint64_t* q_free = q_full + kQueues;             // [kQueues]
     volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + P.misc);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + P.misc + 16);
+    int* qcount = reinterpret_cast<int*>(sm + P.qcount);
+    int* qbase = reinterpret_cast<int*>(sm + P.queue);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         mbar_init(a_full, 1);
-        mbar_init(a_empty, kEpiWarps);
-        for (int s = 0; s < 2; ++s) {
+        mbar_init(a_empty, kFilterWarps);
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(&b_full[s], 1);
-            mbar_init(&b_empty[s], kEpiWarps);
-            mbar_init(&acc_full[s], 1);
-            mbar_init(&acc_empty[s], kEpiWarps);
+            mbar_init(&b_empty[s], kFilterWarps);
         }
-        mbar_init(epi_bar, kEpiWarps);
-        int* qc = reinterpret_cast<int*>(sm + P.qcount);
-        qc[0] = qc[1] = qc[2] = 0;
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&acc_full[s], 1);
+            mbar_init(&acc_empty[s], kFilterWarps);
+        }
+        for (int q = 0; q < kQueues; ++q) {
+            mbar_init(&q_full[q], kFilterWarps);
+            mbar_init(&q_free[q], 1);
+            qcount[q] = 0;
+        }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -363,12 +366,10 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const uint32_t a_bytes = (uint32_t)panels * kRows * 32;
-    const uint32_t b_half_bytes = (uint32_t)panels * kRows * 32;
-    const uint32_t m_block_bytes = a.exact ? (uint32_t)kRows * a.dm * 2 : 0u;
+    const uint32_t a_bytes = (uint32_t)panels * kRows * 32;   // one 128-row block of an image
 
     if (warp == 0) {
-        // ---------------------------------------------------------------- TMA producer
+        // ---------------------------------------------------------------- producer
         if (lane == 0) {
             int g = 0;
             bool ok = true;
@@ -378,48 +379,41 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                 if (!mbar_wait(a_empty, (t & 1) ^ 1, abort_flag, a.err, 1)) { ok = false; break; }
                 tw[0] += clock64() - c0;
                 const int B = a.b_lo + item % a.nb;
-                mbar_expect_tx(a_full, a_bytes + kRows * 4 + m_block_bytes);
+                mbar_expect_tx(a_full, a_bytes + kRows * 4);
                 bulk_load(sm + P.a, a.aimg + (size_t)B * a_bytes, a_bytes, a_full);
-                if (m_block_bytes)
-                    bulk_load(sm + P.am, a.resid + (size_t)B * kRows * a.dm, m_block_bytes, a_full);
                 bulk_load(sm + P.arow_u, a.U + (size_t)B * kRows, kRows * 4, a_full);
                 int p_lo;
                 const int nu = item_units(a, item, p_lo);
                 for (int uix = 0; uix < nu; ++uix, ++g) {
-                    const int s = g & 1;
+                    const int s = g % kStages;
                     c0 = clock64();
-                    if (!mbar_wait(&b_empty[s], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 2)) { ok = false; break; }
+                    if (!mbar_wait(&b_empty[s], ((g / kStages) & 1) ^ 1, abort_flag, a.err, 2)) { ok = false; break; }
                     tw[1] += clock64() - c0;
                     const Unit u = make_unit(a, item, p_lo + uix);
-                    unsigned char* bb = sm + (s ? P.b1 : P.b0);
-                    mbar_expect_tx(&b_full[s], 2 * b_half_bytes + 2 * kRows * 4 + 2 * m_block_bytes);
-                    const int rows0 = (u.R0 >= 0 ? u.R0 * kRows : a.row_pad);
-                    const int rows1 = (u.R1 >= 0 ? u.R1 * kRows : a.row_pad);
-                    const unsigned char* img0 = a.bimg + (size_t)(rows0 / kRows) * b_half_bytes;
-                    const unsigned char* img1 = a.bimg + (size_t)(rows1 / kRows) * b_half_bytes;
+                    unsigned char* bb = sm + P.b[s];
+                    mbar_expect_tx(&b_full[s], 2 * a_bytes + 2 * kRows * 4);
+                    const int blk0 = (u.R0 >= 0 ? u.R0 : a.row_pad / kRows);
+                    const int blk1 = (u.R1 >= 0 ? u.R1 : a.row_pad / kRows);
+                    const unsigned char* img0 = a.bimg + (size_t)blk0 * a_bytes;
+                    const unsigned char* img1 = a.bimg + (size_t)blk1 * a_bytes;
                     for (int p = 0; p < panels; ++p) {
                         bulk_load(bb + p * kCols * 32, img0 + p * kRows * 32, kRows * 32, &b_full[s]);
                         bulk_load(bb + p * kCols * 32 + kRows * 32, img1 + p * kRows * 32, kRows * 32, &b_full[s]);
                     }
-                    bulk_load(sm + P.bcol_u[s], a.U + rows0, kRows * 4, &b_full[s]);
-                    bulk_load(sm + P.bcol_u[s] + kRows * 4, a.U + rows1, kRows * 4, &b_full[s]);
-                    if (m_block_bytes) {
-                        unsigned char* bmd = sm + (s ? P.bm1 : P.bm0);
-                        bulk_load(bmd, a.resid + (size_t)rows0 * a.dm, m_block_bytes, &b_full[s]);
-                        bulk_load(bmd + m_block_bytes, a.resid + (size_t)rows1 * a.dm, m_block_bytes, &b_full[s]);
-                    }
+                    bulk_load(sm + P.bcol_u[s], a.U + (size_t)blk0 * kRows, kRows * 4, &b_full[s]);
+                    bulk_load(sm + P.bcol_u[s] + kRows * 4, a.U + (size_t)blk1 * kRows, kRows * 4, &b_full[s]);
                 }
             }
             if (a.counters) {
                 atomicAdd(&a.counters[4 + kTProdWaitA], (unsigned long long)tw[0]);
                 atomicAdd(&a.counters[4 + kTProdWaitB], (unsigned long long)tw[1]);
             }
-            // on abort, let copies already issued land before the CTA exits (bounded)
+            // on abort, let the copies already issued land before the CTA exits (bounded)
             if (!ok) {
                 const long long t0 = clock64();
-                for (int q = 0; q < 2 && q < g; ++q) {
+                for (int q = 0; q < kStages && q < g; ++q) {
                     const int gl = g - 1 - q;
-                    while (!mbar_try_wait(&b_full[gl & 1], (gl >> 1) & 1) && clock64() - t0 < kWaitCycles) {
+                    while (!mbar_try_wait(&b_full[gl % kStages], (gl / kStages) & 1) && clock64() - t0 < kWaitCycles) {
                     }
                 }
             }
@@ -438,20 +432,20 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                 int p_lo;
                 const int nu = item_units(a, item, p_lo);
                 for (int uix = 0; uix < nu; ++uix, ++g) {
-                    const int s = g & 1;
+                    const int s = g % kStages, acc = g & 1;
                     c0 = clock64();
-                    if (!mbar_wait(&b_full[s], (g >> 1) & 1, abort_flag, a.err, 4)) { ok = false; break; }
-                    long long c1 = clock64();
+                    if (!mbar_wait(&b_full[s], (g / kStages) & 1, abort_flag, a.err, 4)) { ok = false; break; }
+                    const long long c1 = clock64();
                     tw[1] += c1 - c0;
-                    if (!mbar_wait(&acc_empty[s], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 5)) { ok = false; break; }
+                    if (!mbar_wait(&acc_empty[acc], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 5)) { ok = false; break; }
                     tw[2] += clock64() - c1;
                     tc_fence_after();
-                    const uint32_t d_tmem = tmem_base + (uint32_t)(s * kCols);
-                    const uint32_t abase = su32(sm + P.a), bbase = su32(sm + (s ? P.b1 : P.b0));
+                    const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kCols);
+                    const uint32_t abase = su32(sm + P.a), bbase = su32(sm + P.b[s]);
                     for (int p = 0; p < panels; ++p)
                         mma_tf32(d_tmem, sw32_desc(abase + p * kRows * 32), sw32_desc(bbase + p * kCols * 32),
                                  p > 0 ? 1u : 0u);
-                    mma_commit(&acc_full[s]);
+                    mma_commit(&acc_full[acc]);
                 }
             }
             if (a.counters) {
@@ -461,60 +455,42 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
             }
         }
         __syncwarp();
-    } else {
-        // ---------------------------------------------------------------- epilogue
+    } else if (warp < 2 + kFilterWarps) {
+        // ---------------------------------------------------------------- filter
         const int e = warp - 2;                 // 0..7
-        const int quad = warp & 3;              // TMEM lanes this warp may read
+        const int quad = warp & 3;              // the TMEM lane quarter this warp may read
         const int half = e >> 2;                // column half of the tile
         const int ra = quad * 32 + lane;        // this thread's A row (tile-local)
-        const int16_t* am = reinterpret_cast<const int16_t*>(sm + P.am);
-        uint32_t* queues = reinterpret_cast<uint32_t*>(sm + P.queue);
-        int* qcount = reinterpret_cast<int*>(sm + P.qcount);
         int g = 0;
         bool ok = true;
-        long long te[4] = {0, 0, 0, 0};
+        long long tw[2] = {0, 0};
+        unsigned long long inline_entries = 0;
         for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
             if (!mbar_wait(a_full, t & 1, abort_flag, a.err, 6)) { ok = false; break; }
             const float Ui = reinterpret_cast<const float*>(sm + P.arow_u)[ra];
             int p_lo;
             const int nu = item_units(a, item, p_lo);
             for (int uix = 0; uix < nu; ++uix, ++g) {
-                const int s = g & 1, qi = g % 3;
-                long long c0 = clock64();
-                if (!mbar_wait(&acc_full[s], (g >> 1) & 1, abort_flag, a.err, 7)) { ok = false; break; }
-                long long c1 = clock64();
-                te[0] += c1 - c0;
+                const int s = g % kStages, acc = g & 1, qi = g % kQueues;
+                const long long c0 = clock64();
+                if (!mbar_wait(&acc_full[acc], (g >> 1) & 1, abort_flag, a.err, 7)) { ok = false; break; }
+                if (!mbar_wait(&q_free[qi], ((g / kQueues) & 1) ^ 1, abort_flag, a.err, 8)) { ok = false; break; }
+                const long long c1 = clock64();
+                tw[0] += c1 - c0;
                 tc_fence_after();
                 const Unit u = make_unit(a, item, p_lo + uix);
                 const int gi = u.B * kRows + ra;
                 const bool row_real = gi < a.n;
-                const unsigned char* bb = sm + (s ? P.b1 : P.b0);
-                const int16_t* bm = reinterpret_cast<const int16_t*>(sm + (s ? P.bm1 : P.bm0));
                 const float* cu = reinterpret_cast<const float*>(sm + P.bcol_u[s]);
-                uint32_t* qmeta = queues + qi * 3 * kQueueCap;
-                uint32_t* qrow = qmeta + kQueueCap;
-                uint32_t* qcol = qrow + kQueueCap;
+                int* qgi = qbase + qi * 4 * kQueueCap;
+                int* qgj = qgi + kQueueCap;
+                unsigned* qmr = reinterpret_cast<unsigned*>(qgj + kQueueCap);
+                unsigned* qmc = qmr + kQueueCap;
                 const int rblk = half ? u.R1 : u.R0;
-                // ---- phase 1: filter the accumulator, queue the survivors
-                // one pair's survivors, handled in place (queue full, or TF32 mode where acc is the d2)
-                auto settle = [&](int c, int q, bool row_hit, bool col_hit, float accv) {
-                    const int jloc = half * 128 + c * 32 + q;
-                    const int gj = rblk * kRows + c * 32 + q;
-                    if (gj == gi || gj >= a.n) return;
-                    const float d2 = a.exact ? refine_d2(sm + P.a, am, ra, bb, bm, jloc, a.d, a.dm, a.nrm[gi], a.nrm[gj])
-                                             : fmaxf(accv, 0.0f);
-                    if (row_hit) {
-                        const uint64_t key = pack_key(d2, gj);
-                        if (key < a.thr[gi]) tc_append(a, gi, key);
-                    }
-                    if (col_hit) {
-                        const uint64_t key = pack_key(d2, gi);
-                        if (key < a.thr[gj]) tc_append(a, gj, key);
-                    }
-                };
                 auto process = [&](const uint32_t (&rv)[32], int c) {
                     const int cb = half * 128 + c * 32;
-                    unsigned mrow = 0, mcol = 0;
+                    // four independent partial masks keep the dependency chains short
+                    unsigned mr[4] = {0, 0, 0, 0}, mc[4] = {0, 0, 0, 0};
 #pragma unroll
                     for (int q = 0; q < 32; q += 4) {
                         const float4 u4 = *reinterpret_cast<const float4*>(cu + cb + q);
@@ -522,108 +498,128 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
 #pragma unroll
                         for (int w = 0; w < 4; ++w) {
                             const float v = __uint_as_float(rv[q + w]);
-                            if (v <= Ui) mrow |= 1u << (q + w);
-                            if (v <= uc[w]) mcol |= 1u << (q + w);
+                            if (v <= Ui) mr[w] |= 1u << (q + w);
+                            if (v <= uc[w]) mc[w] |= 1u << (q + w);
                         }
                     }
+                    unsigned mrow = (mr[0] | mr[1]) | (mr[2] | mr[3]);
+                    unsigned mcol = (mc[0] | mc[1]) | (mc[2] | mc[3]);
                     if (!row_real) mrow = 0;
-                    if (!row_real || a.diag) mcol = 0;   // diagonal units: both orders are rows
-                    const unsigned m = mrow | mcol;
-                    if (!__any_sync(0xffffffffu, m != 0u)) return;
+                    if (!row_real || a.diag) mcol = 0;   // diagonal tiles: both orders appear as rows
+                    if (!__any_sync(0xffffffffu, (mrow | mcol) != 0u)) return;
+                    const int gj0 = rblk * kRows + c * 32;
                     if (!a.exact) {
-                        float* scr = reinterpret_cast<float*>(sm + P.am) + e * 32 * 33;
+                        // precision TF32: the accumulator is the distance, admit right here
+                        const unsigned mm = mrow | mcol;
+                        if (mm) {
 #pragma unroll
-                        for (int q = 0; q < 32; ++q) scr[lane * 33 + q] = __uint_as_float(rv[q]);
-                        for (unsigned mm = m; mm; mm &= mm - 1) {
-                            const int q = __ffs(mm) - 1;
-                            settle(c, q, (mrow >> q) & 1u, (mcol >> q) & 1u, scr[lane * 33 + q]);
+                            for (int q = 0; q < 32; ++q) {
+                                if (!((mm >> q) & 1u)) continue;
+                                const int gj = gj0 + q;
+                                if (gj == gi || gj >= a.n) continue;
+                                const float d2 = fmaxf(__uint_as_float(rv[q]), 0.0f);
+                                if ((mrow >> q) & 1u) {
+                                    const uint64_t key = pack_key(d2, gj);
+                                    if (key < __ldg(a.thr + gi)) tc_append(a, gi, key);
+                                }
+                                if ((mcol >> q) & 1u) {
+                                    const uint64_t key = pack_key(d2, gi);
+                                    if (key < __ldg(a.thr + gj)) tc_append(a, gj, key);
+                                }
+                            }
                         }
-                    } else if (m) {
+                    } else if (mrow | mcol) {
                         const int slot = atomicAdd(&qcount[qi], 1);
                         if (slot < kQueueCap) {
-                            qmeta[slot] = (uint32_t)ra | ((uint32_t)c << 8) | ((uint32_t)half << 10);
-                            qrow[slot] = mrow;
-                            qcol[slot] = mcol;
+                            qgi[slot] = gi;
+                            qgj[slot] = gj0;
+                            qmr[slot] = mrow;
+                            qmc[slot] = mcol;
                         } else {
-                            for (unsigned mm = m; mm; mm &= mm - 1) {
-                                const int q = __ffs(mm) - 1;
-                                settle(c, q, (mrow >> q) & 1u, (mcol >> q) & 1u, 0.0f);
-                            }
+                            // queue full (dense early rounds): refine in place
+                            settle_exact(a, gi, gj0, mrow, mcol);
+                            ++inline_entries;
                         }
                     }
                     __syncwarp();
                 };
                 if (rblk >= 0) {
                     // two chunks in flight: the TMEM load of chunk c + 1 overlaps the filter of chunk c
-                    const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(s * kCols + half * 128);
-                    uint32_t ra0[32], ra1[32];
-                    tmem_ld32(tbase, ra0);
-                    tmem_wait(ra0);
-                    tmem_ld32(tbase + 32, ra1);
-                    process(ra0, 0);
-                    tmem_wait(ra1);
-                    tmem_ld32(tbase + 64, ra0);
-                    process(ra1, 1);
-                    tmem_wait(ra0);
-                    tmem_ld32(tbase + 96, ra1);
-                    process(ra0, 2);
-                    tmem_wait(ra1);
-                    process(ra1, 3);
+                    const uint32_t tbase =
+                        tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * kCols + half * 128);
+                    uint32_t r0[32], r1[32];
+                    tmem_ld32(tbase, r0);
+                    tmem_wait(r0);
+                    tmem_ld32(tbase + 32, r1);
+                    process(r0, 0);
+                    tmem_wait(r1);
+                    tmem_ld32(tbase + 64, r0);
+                    process(r1, 1);
+                    tmem_wait(r0);
+                    tmem_ld32(tbase + 96, r1);
+                    process(r0, 2);
+                    tmem_wait(r1);
+                    process(r1, 3);
                 }
-                // the accumulator is no longer needed: let the MMA of a later tile reuse it
+                // the accumulator and the B stage are done with: release both, hand the queue over
+                // (the proxy fence orders this warp's reads of the stage before the next bulk copy)
                 tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[s]);
-                // queue (g + 1) % 3 last served tile g - 2, which every warp finished before the
-                // previous barrier; reset it before this barrier so tile g + 1 starts empty
-                if (e == 0 && lane == 0) qcount[(g + 1) % 3] = 0;
-                __syncwarp();
-                long long c2 = clock64();
-                te[1] += c2 - c1;
-                if (lane == 0) mbar_arrive(epi_bar);
-                if (!mbar_wait(epi_bar, g & 1, abort_flag, a.err, 8)) { ok = false; break; }
-                long long c3 = clock64();
-                te[2] += c3 - c2;
-                // ---- phase 2: refine the queued survivors; entries are dealt round-robin to the warps
-                const int nq = min(qcount[qi], kQueueCap);
-                for (int ei = lane * kEpiWarps + e; ei < nq; ei += 32 * kEpiWarps) {
-                    const uint32_t meta = qmeta[ei];
-                    const int qrw = meta & 0xFF, c = (meta >> 8) & 3;
-                    const unsigned mr = qrow[ei], mc = qcol[ei];
-                    const int gi2 = u.B * kRows + qrw;
-                    // this entry's chunk and half follow from the warp that queued it: c is the chunk,
-                    // the half is stored in bit 10
-                    const int hf = (meta >> 10) & 1;
-                    const int rb2 = hf ? u.R1 : u.R0;
-                    for (unsigned mm = mr | mc; mm; mm &= mm - 1) {
-                        const int q = __ffs(mm) - 1;
-                        const int jloc = hf * 128 + c * 32 + q;
-                        const int gj = rb2 * kRows + c * 32 + q;
-                        if (gj == gi2 || gj >= a.n) continue;
-                        const float d2 = refine_d2(sm + P.a, am, qrw, bb, bm, jloc, a.d, a.dm, a.nrm[gi2], a.nrm[gj]);
-                        if ((mr >> q) & 1u) {
-                            const uint64_t key = pack_key(d2, gj);
-                            if (key < a.thr[gi2]) tc_append(a, gi2, key);
-                        }
-                        if ((mc >> q) & 1u) {
-                            const uint64_t key = pack_key(d2, gi2);
-                            if (key < a.thr[gj]) tc_append(a, gj, key);
-                        }
-                    }
-                }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
-                te[3] += clock64() - c3;
-                if (lane == 0) mbar_arrive(&b_empty[s]);
+                tw[1] += clock64() - c1;
+                if (lane == 0) {
+                    mbar_arrive(&acc_empty[acc]);
+                    mbar_arrive(&b_empty[s]);
+                    mbar_arrive(&q_full[qi]);
+                }
             }
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(a_empty);
         }
+        if (a.counters) {
+            if (inline_entries) atomicAdd(&a.counters[1], inline_entries);
+            if (lane == 0) {
+                atomicAdd(&a.counters[4 + kTFiltWait], (unsigned long long)tw[0]);
+                atomicAdd(&a.counters[4 + kTFiltWork], (unsigned long long)tw[1]);
+            }
+        }
+    } else {
+        // ---------------------------------------------------------------- refine
+        const int r = warp - 2 - kFilterWarps;   // 0 .. kRefineWarps - 1
+        int g = 0;
+        bool ok = true;
+        long long tw[2] = {0, 0};
+        unsigned long long entries = 0;
+        for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
+            int p_lo;
+            const int nu = item_units(a, item, p_lo);
+            for (int uix = 0; uix < nu; ++uix, ++g) {
+                if (g % kRefineWarps != r) continue;
+                const int qi = g % kQueues;
+                const long long c0 = clock64();
+                if (!mbar_wait(&q_full[qi], (g / kQueues) & 1, abort_flag, a.err, 9)) { ok = false; break; }
+                const long long c1 = clock64();
+                tw[0] += c1 - c0;
+                const int* qgi = qbase + qi * 4 * kQueueCap;
+                const int* qgj = qgi + kQueueCap;
+                const unsigned* qmr = reinterpret_cast<const unsigned*>(qgj + kQueueCap);
+                const unsigned* qmc = qmr + kQueueCap;
+                const int nq = min(qcount[qi], kQueueCap);
+                entries += nq;
+                for (int ei = lane; ei < nq; ei += 32) settle_exact(a, qgi[ei], qgj[ei], qmr[ei], qmc[ei]);
+                __syncwarp();
+                tw[1] += clock64() - c1;
+                if (lane == 0) {
+                    qcount[qi] = 0;
+                    mbar_arrive(&q_free[qi]);
+                }
+                __syncwarp();
+            }
+        }
         if (a.counters && lane == 0) {
-            atomicAdd(&a.counters[4 + kTEpiWaitAcc], (unsigned long long)te[0]);
-            atomicAdd(&a.counters[4 + kTEpiP1], (unsigned long long)te[1]);
-            atomicAdd(&a.counters[4 + kTEpiBar], (unsigned long long)te[2]);
-            atomicAdd(&a.counters[4 + kTEpiP2], (unsigned long long)te[3]);
+            atomicAdd(&a.counters[0], entries);
+            atomicAdd(&a.counters[4 + kTRefWait], (unsigned long long)tw[0]);
+            atomicAdd(&a.counters[4 + kTRefWork], (unsigned long long)tw[1]);
         }
     }
 
@@ -659,23 +655,24 @@ __device__ __forceinline__ size_t image_offset(int i, int k, int kp)
     return (size_t)blk * (kp / 8) * 4096 + (size_t)p * 4096 + (size_t)r * 32 + phys * 16 + (c & 3) * 4;
 }
 
-// One thread per row: TF32-rounded A / B operand rows, residuals, and poison for padding rows
-// (their product with any real row is 2^100, above every finite bound).
-__global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, int d, int kp, int dm,
+// One thread per row: TF32-rounded A / B operand rows, the original coordinates point-major (zero
+// padded to dp), and poison for padding rows (their product with any real row is 2^100, above every
+// finite bound).
+__global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, int d, int kp, int dp,
                                   int rows_a, int rows_b, unsigned char* __restrict__ A,
-                                  unsigned char* __restrict__ Bm, int16_t* __restrict__ resid)
+                                  unsigned char* __restrict__ Bm, float* __restrict__ xp)
 {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= rows_b) return;
     const bool has_a = i < rows_a;
-    int16_t* mrow = resid + (size_t)i * dm;
+    float* xr = xp + (size_t)i * dp;
     auto put = [&](unsigned char* img, int k, float v) { *reinterpret_cast<float*>(img + image_offset(i, k, kp)) = v; };
     if (i >= n) {
         for (int k = 0; k < kp; ++k) {
             if (has_a) put(A, k, (k == d + 3) ? kPoisonNorm : 0.0f);
             put(Bm, k, (k == d) ? kPoisonNorm : 0.0f);
         }
-        for (int k = 0; k < dm; ++k) mrow[k] = 0;
+        for (int k = 0; k < dp; ++k) xr[k] = 0.0f;
         return;
     }
     float nt = 0.0f;
@@ -685,9 +682,9 @@ __global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, i
         nt = __fmaf_rn(xt, xt, nt);
         if (has_a) put(A, k, __fmul_rn(-2.0f, xt));
         put(Bm, k, xt);
-        mrow[k] = (int16_t)(__float_as_int(xv) - __float_as_int(xt));
+        xr[k] = xv;
     }
-    for (int k = d; k < dm; ++k) mrow[k] = 0;
+    for (int k = d; k < dp; ++k) xr[k] = 0.0f;
     float h, m, l;
     split3(nt, h, m, l);
     const float av[6] = {1.0f, 1.0f, 1.0f, h, m, l};
@@ -705,13 +702,11 @@ __global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, i
 namespace {
 
 struct TcState {
-    int device = -1, n = 0, d = 0, kp = 0, npad = 0;
-    const float* x = nullptr;
-    float *A = nullptr, *B = nullptr, *U = nullptr, *nrm = nullptr;   // U/nrm/thr: scheduler-owned
-    int16_t* resid = nullptr;
-    int dm = 0;
+    int n = 0, d = 0, kp = 0, dp = 0, npad = 0, sms = 0;
+    unsigned char *A = nullptr, *B = nullptr;
+    float* xp = nullptr;
+    float *U = nullptr, *nrm = nullptr;   // U / nrm / thr belong to the scheduler
     uint64_t* thr = nullptr;
-    int sms = 0;
 };
 
 TcState g_state;   // the prepared operands of the current kNN call (one per process)
@@ -725,43 +720,40 @@ bool tc_engine_supported(int d)
     cudaDeviceProp p;
     if (cudaGetDeviceProperties(&p, dev) != cudaSuccess) return false;
     const int kp = tc_kp(d);
-    const int dm = ((d + 7) / 8) * 8;
-    return p.major == 10 && p.minor == 0 && kp <= tc::kMaxKp && tc::smem_plan(kp, dm).total + 1024 <= 227 * 1024;
+    return p.major == 10 && p.minor == 0 && kp <= tc::kMaxKp && tc::smem_plan(kp).total + 1024 <= 227 * 1024;
 }
 
-// Prepares the TF32 operand rows and tensor maps for one kNN call; the per-point bounds,
-// norms and thresholds (rows_b entries each) belong to the scheduler.
+// Prepares the TF32 operand images and the point-major original coordinates for one kNN call; the
+// per-point bounds, norms and thresholds (Npad + 128 entries each) belong to the scheduler.
 void tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const float* norms, const float* U,
                 const uint64_t* thr, cudaStream_t s)
 {
     TcState& st = g_state;
     const int kp = tc_kp(d);
-    const int dm = ((d + 7) / 8) * 8;
+    const int dp = ((d + 3) / 4) * 4;
     const int T = (n + kBlock - 1) / kBlock;
     const int npad = T * kBlock;
     const int rows_b = npad + kBlock;     // + one poison block
     const size_t a_bytes = sizeof(float) * (size_t)npad * kp;
     const size_t b_bytes = sizeof(float) * (size_t)rows_b * kp;
-    const size_t m_bytes = sizeof(int16_t) * (size_t)rows_b * dm;
-    char* mem = (char*)ws.ops.ensure(a_bytes + b_bytes + m_bytes + 3072);
+    const size_t x_bytes = sizeof(float) * (size_t)rows_b * dp;
+    char* mem = (char*)ws.ops.ensure(a_bytes + b_bytes + x_bytes + 3072);
     auto align = [](char* p) { return (char*)(((uintptr_t)p + 1023) & ~(uintptr_t)1023); };
-    st.A = (float*)align(mem);
-    st.B = (float*)align((char*)st.A + a_bytes);
-    st.resid = (int16_t*)align((char*)st.B + b_bytes);
+    st.A = (unsigned char*)align(mem);
+    st.B = (unsigned char*)align((char*)st.A + a_bytes);
+    st.xp = (float*)align((char*)st.B + b_bytes);
     // the images have no gaps: every element is written by the build kernel
-    tc::build_rows_kernel<<<(rows_b + 127) / 128, 128, 0, s>>>(x, ldx, n, d, kp, dm, npad, rows_b,
-                                                               (unsigned char*)st.A, (unsigned char*)st.B, st.resid);
+    tc::build_rows_kernel<<<(rows_b + 127) / 128, 128, 0, s>>>(x, ldx, n, d, kp, dp, npad, rows_b, st.A, st.B,
+                                                               st.xp);
     FDB_LAUNCHED();
     int dev = 0;
     FDB_CUDA(cudaGetDevice(&dev));
     FDB_CUDA(cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev));
-    st.device = dev;
     st.n = n;
     st.d = d;
     st.kp = kp;
-    st.dm = dm;
+    st.dp = dp;
     st.npad = npad;
-    st.x = x;
     st.U = const_cast<float*>(U);
     st.nrm = const_cast<float*>(norms);
     st.thr = const_cast<uint64_t*>(thr);
@@ -775,10 +767,7 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.n = r.n;
     a.d = r.d;
     a.kp = st.kp;
-    a.dm = st.dm;
-    a.resid = st.resid;
-    a.aimg = (const unsigned char*)st.A;
-    a.bimg = (const unsigned char*)st.B;
+    a.dp = st.dp;
     a.T = r.T;
     a.b_lo = r.b_lo;
     a.nb = r.nb;
@@ -791,6 +780,9 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.U = st.U;
     a.nrm = st.nrm;
     a.thr = st.thr;
+    a.xp = st.xp;
+    a.aimg = st.A;
+    a.bimg = st.B;
     a.cand = r.cand;
     a.cnt = r.cnt;
     a.ovf = r.ovf;
@@ -810,7 +802,7 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
         a.items = r.nb * ((a.npairs + ppi - 1) / ppi);
     }
     if (a.items <= 0) return;
-    const tc::Smem P = tc::smem_plan(st.kp, st.dm);
+    const tc::Smem P = tc::smem_plan(st.kp);
     const size_t smem = P.total + 1024;
     static bool attr_set = false;
     if (!attr_set) {
