@@ -115,9 +115,15 @@ void compute_norms(const float* x, int ldx, int n, int d, float* norms, cudaStre
 
 // true when the tcgen05 tile engine can run this shape on the current device
 bool tc_engine_supported(int d);
-// builds the tcgen05 operands (point-major augmented rows) and their tensor maps
-void tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const float* norms, const float* U,
-                const uint64_t* thr, cudaStream_t s);
+// where the list merge writes each point's folded filter bound for the tcgen05 engine: the A
+// operand image (w parts of every row) and the TF32 norms the fold needs
+struct TcFold {
+    unsigned char* aimg = nullptr;
+    const float* ntf = nullptr;
+};
+// builds the tcgen05 operand images (pre-swizzled augmented rows) and the exact point-major copy
+TcFold tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const float* norms, const float* U,
+                  const uint64_t* thr, cudaStream_t s);
 
 // ---------------------------------------------------------------- density / detection
 // Sequential-order double mean of the first k ranks (rank stride n) -- bit-identical to the

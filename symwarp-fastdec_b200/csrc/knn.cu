@@ -180,12 +180,14 @@ __host__ __device__ inline int next_pow2(int v)
 }
 
 // one warp per point: list <- k-smallest of (list, new candidates); threshold <- list[k-1];
-// filter bound U <- threshold plus the TF32 margin (filter_bound)
+// with the tcgen05 engine also the filter bound: U <- V and the A operand row's w parts
+// (fold_bound of the threshold plus the TF32 margin)
 __global__ void knn_merge_kernel(uint64_t* __restrict__ lists, uint64_t* __restrict__ thr,
                                  float* __restrict__ U, const float* __restrict__ norms,
                                  const uint64_t* __restrict__ cand, int* __restrict__ cnt, int n,
                                  int k, int cap, int pw, int d, int kp, int exact,
-                                 unsigned long long* __restrict__ admitted)
+                                 unsigned long long* __restrict__ admitted, unsigned char* __restrict__ aimg,
+                                 const float* __restrict__ ntf)
 {
     extern __shared__ uint64_t msm[];
     const int warps = blockDim.x >> 5, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -209,7 +211,12 @@ __global__ void knn_merge_kernel(uint64_t* __restrict__ lists, uint64_t* __restr
         thr[p] = t;
         cnt[p] = 0;
         const float T = (t == kEmptyKey) ? __int_as_float(0x7f800000) : __uint_as_float((uint32_t)(t >> 32));
-        U[p] = filter_bound(T, norms[p], d, kp, exact);
+        if (aimg) {
+            float V, w;
+            fold_bound(filter_bound(T, norms[p], d, kp, exact), ntf[p], kp, exact, V, w);
+            U[p] = V;
+            store_fold(aimg, p, d, kp, w);
+        }
         atomicAdd(admitted, (unsigned long long)c);
     }
 }
@@ -382,7 +389,8 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     res.engine_used = engine;
     const int kp = tc_kp(d);
     const int exact = cfg.precision == FDB200_FP32 ? 1 : 0;
-    if (engine == FDB200_ENGINE_TCGEN05) tc_prepare(ws, x, cfg.ldx, n, d, norms, U, thr, s);
+    TcFold fold;
+    if (engine == FDB200_ENGINE_TCGEN05) fold = tc_prepare(ws, x, cfg.ldx, n, d, norms, U, thr, s);
 
     int mwarps;
     size_t msmem;
@@ -456,7 +464,7 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
             continue;
         }
         knn_merge_kernel<<<(n + mwarps - 1) / mwarps, mwarps * 32, msmem, s>>>(
-            lists, thr, U, norms, cand, cnt, n, k, cap, pw, d, kp, exact, admitted);
+            lists, thr, U, norms, cand, cnt, n, k, cap, pw, d, kp, exact, admitted, fold.aimg, fold.ntf);
         FDB_LAUNCHED();
         if (trace) {
             unsigned long long adm = 0, cn[16] = {0};
@@ -472,8 +480,8 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
                     100.0 * cn[1] / chunks, cn[1] ? (double)cn[2] / cn[1] : 0.0);
             adm_before = adm;
             if (engine == FDB200_ENGINE_TCGEN05 && !r.diag) {
-                // per tcgen05 tile (= two offsets), cycles per CTA role instance
-                const double tiles = (double)units / 2.0;
+                // per tcgen05 tile (counted by the MMA issuers), cycles per CTA role instance
+                const double tiles = cn[3] > 0 ? (double)cn[3] : 1.0;
                 const double per_f = tiles * 8.0;   // filter warp-tiles (each tile has one refine warp)
                 fprintf(stderr, "[fdb200]   cycles/tile: prod wait A %.0f B %.0f | mma wait A %.0f B %.0f acc %.0f |"
                                 " filter wait %.0f work %.0f | refine wait %.0f work %.0f | entries/tile %.1f"

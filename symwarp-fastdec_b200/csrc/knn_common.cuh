@@ -22,7 +22,7 @@ struct TileRound {
     int ldx, n, d;
     const float* norms;
     const uint64_t* thr;     // per-point admission bound: a key is admitted iff key < thr
-    const float* U;          // per-point TF32 filter bound (tcgen05 engine)
+    const float* U;          // per-point folded filter bound V (tcgen05 engine)
     uint64_t* cand;          // n * cap candidate slots
     int* cnt;                // per-point slot counters
     int cap;
@@ -100,6 +100,61 @@ __device__ __forceinline__ float filter_bound(float T, float ni, int d, int kp, 
     const double E = c_ref * (n + b * b) + 2.0 * R * eps * (a + b) + eps * eps * (a + b) * (a + b) +
                      c_acc * 2.0 * (nt_i + nt_j) + c_nrm * (nt_i + nt_j);
     return __double2float_ru(t + E);
+}
+
+// byte offset of element k of row i inside a blocked, pre-swizzled tcgen05 operand image: 128-row
+// blocks of K/8 panels, each panel 128 rows x 32 bytes with the SWIZZLE_32B chunk order, so one
+// contiguous bulk copy of a panel lands in shared memory exactly as the MMA descriptor expects it
+__host__ __device__ __forceinline__ size_t image_offset(int i, int k, int kp)
+{
+    const int blk = i >> 7, r = i & 127, p = k >> 3, c = k & 7;
+    const int phys = ((c >> 2) ^ ((r >> 2) & 1));
+    return (size_t)blk * (kp / 8) * 4096 + (size_t)p * 4096 + (size_t)r * 32 + phys * 16 + (c & 3) * 4;
+}
+
+// v = h + m + l exactly, each part exact in TF32 (11 significant bits, then 11, then at most 2)
+__device__ __forceinline__ void split3(float v, float& h, float& m, float& l)
+{
+    h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+    const float r = __fsub_rn(v, h);
+    m = __uint_as_float(__float_as_uint(r) & 0xFFFFE000u);
+    l = __fsub_rn(r, m);
+}
+
+// The tcgen05 engine folds point i's filter bound into its A operand row: the three "norm of i"
+// entries hold w_i = n~_i - V_i instead, so the MMA yields acc'(i, j) = |x~_i - x~_j|^2 - V_i and a
+// candidate survives iff acc' is negative (its sign bit). With U = filter_bound(T) covering the
+// accumulation error of the plain sum, the extra term w_i adds at most c_acc |w_i| <= c_acc (n~ + V)
+// of error; V also adds 2^-100 so that a survivor's acc' is strictly below zero. Infinite bounds
+// (empty lists) become w = -2^120: everything survives. Precision TF32 folds the plain threshold.
+constexpr float kFoldAll = -1.329227995784916e36f;   // -2^120, exact in TF32
+
+__device__ __forceinline__ void fold_bound(float U, float nt, int kp, int exact, float& V, float& w)
+{
+    if (!(U < __int_as_float(0x7f800000))) {
+        V = __int_as_float(0x7f800000);
+        w = kFoldAll;
+        return;
+    }
+    if (!exact) {
+        V = U;
+        w = __fsub_rn(nt, U);
+        return;
+    }
+    const float c_acc = (float)(kp / 8) * 0x1p-20f * 1.01f;
+    V = __fadd_ru(U, __fmul_ru(c_acc, __fadd_ru(nt, U)));
+    V = __fadd_ru(V, 0x1p-100f);
+    w = __fsub_rd(nt, V);
+}
+
+// writes w's three TF32 parts into row i of the A operand image (columns d + 3 .. d + 5)
+__device__ __forceinline__ void store_fold(unsigned char* aimg, int i, int d, int kp, float w)
+{
+    float h, m, l;
+    split3(w, h, m, l);
+    *reinterpret_cast<float*>(aimg + image_offset(i, d + 3, kp)) = h;
+    *reinterpret_cast<float*>(aimg + image_offset(i, d + 4, kp)) = m;
+    *reinterpret_cast<float*>(aimg + image_offset(i, d + 5, kp)) = l;
 }
 
 void launch_tile_round_simt(const TileRound& r, int units, cudaStream_t s);

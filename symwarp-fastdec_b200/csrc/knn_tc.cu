@@ -5,29 +5,38 @@
 //
 //   1. TF32 filter on the tensor cores. Every coordinate is rounded to TF32 (nearest) once,
 //      x~ = rna(x), and each point is stored twice, K = D + 6 padded to 8:
-//          A row i = [-2 x~_i, 1, 1, 1, nh_i, nm_i, nl_i, 0...]
-//          B row j = [x~_j, nh_j, nm_j, nl_j, 1, 1, 1, 0...]
-//      with nh + nm + nl = |x~|^2 (fmaf chain) split into three TF32-exact parts. Every operand is
-//      exactly representable in TF32, so the 128 x 256 x K TF32 MMA gives
-//      acc(i, j) = |x~_i - x~_j|^2 up to FP32 accumulation, straight in TMEM.
-//   2. Rigorous margin (filter_bound in knn_common.cuh): a candidate that can still enter point
-//      i's list always has acc <= U_i, so filtering on acc <= U never changes the result.
-//   3. Exact refine. A pair passing acc <= U_row or acc <= U_col is recomputed with the sequential
-//      fmaf chain on the ORIGINAL FP32 coordinates (a point-major copy in global memory) and
-//      admitted with the exact lexicographic test. Precision TF32 skips the refine and keeps
-//      d2 = max(acc, 0).
+//          A row i = [-2 x~_i, 1, 1, 1, wh_i, wm_i, wl_i, 0...]     (rows: the points tested)
+//          B row j = [x~_j, nh_j, nm_j, nl_j, 1, 1, 1, 0...]        (columns: their candidates)
+//      where nh + nm + nl = |x~_j|^2 (fmaf chain) and wh + wm + wl = w_i = |x~_i|^2 - V_i, each
+//      split into three TF32-exact parts (fold_bound in knn_common.cuh). Every operand is exact in
+//      TF32, so the 128 x 256 x K TF32 MMA gives acc'(i, j) = |x~_i - x~_j|^2 - V_i up to FP32
+//      accumulation, straight in TMEM.
+//   2. Rigorous margin: V_i covers the TF32 rounding of the coordinates, the reference's own FP32
+//      rounding and the accumulation error (filter_bound, fold_bound), so every candidate that can
+//      still enter point i's list has acc' < 0. The filter is the sign bit: a 3-input OR over the
+//      raw accumulator words finds the 32-column chunks that hold a survivor, about half an
+//      instruction per pair.
+//   3. Exact refine. A survivor is recomputed with the sequential fmaf chain on the ORIGINAL FP32
+//      coordinates (a point-major copy in global memory) and admitted with the exact lexicographic
+//      test. Precision TF32 keeps d2 = max(acc' + V_i, 0) instead.
 //
-// Kernel shape (persistent, one CTA per SM, 13 warps):
-//   warp 0       producer: cp.async.bulk copies of the A tile (128 rows, resident for a work item)
-//                and of three B stages (two 128-point blocks = 256 rows each), stored in global
-//                memory as pre-swizzled 4 KB K panels (the SWIZZLE_32B K-major layout), plus the
-//                filter bounds of the tile's rows and columns
+// Schedule: the engine visits ORDERED block pairs and tests rows only. A round with offsets
+// [a, a + L) covers, for every row block X, the column blocks X + delta and X - delta (mod T) for
+// each delta in the range (T/2 once when T is even), i.e. exactly the candidates the symmetric SIMT
+// round offers every point. A tile is one row block X against two adjacent column blocks
+// (Y, Y + 1) = (X + delta, X + delta + 1); a work item keeps (Y, Y + 1) resident in shared memory
+// and streams the row blocks X = Y - delta, so per 32768 pairs only one 28 KB row block moves.
+//
+// Kernel shape (persistent, one CTA per SM, 16 warps):
+//   warp 0       producer: cp.async.bulk copies of the resident column pair (pre-swizzled 4 KB K
+//                panels in global memory, the SWIZZLE_32B K-major layout) and of up to four row
+//                block stages
 //   warp 1       TMEM owner and MMA issuer (one thread): K/8 tcgen05.mma kind::tf32 per tile into
-//                one of two 256-column TMEM accumulators, tcgen05.commit to an mbarrier
-//   warps 2..9   filter: tcgen05.ld 32 columns at a time (two loads in flight), two-sided bound
-//                test into per-row survivor masks, one queue entry per (row, 32 columns) with
-//                survivors; then the accumulator and the B stage are released at once
-//   warps 10..12 refine: warp r owns the tiles g = r mod 3 and drains their queues (exact refine
+//                one of two 256-column TMEM accumulators; tcgen05.commit frees the row stage and
+//                publishes the accumulator
+//   warps 2..9   filter: tcgen05.ld 32 columns at a time (two loads in flight), sign-bit test,
+//                survivor masks into a per-tile queue; then the accumulator is released
+//   warps 10..15 refine: warp r owns the tiles g = r mod 6 and drains their queues (exact refine
 //                from global memory, admission, append), off the filter's critical path
 // Every mbarrier wait is bounded (about a second); on a timeout the CTA records an error code,
 // stops issuing work, frees its TMEM and returns, and the host reports the failure.
@@ -42,27 +51,30 @@ namespace fdb {
 namespace tc {
 
 constexpr int kFilterWarps = 8;
-constexpr int kRefineWarps = 3;
+constexpr int kRefineWarps = 6;
 constexpr int kThreads = 32 * (2 + kFilterWarps + kRefineWarps);
-constexpr int kRows = 128;               // A rows per tile
-constexpr int kCols = 256;               // B rows per tile (two blocks)
-constexpr int kStages = 3;               // B stages in shared memory
-constexpr int kQueues = 4;               // survivor queues between filter and refine warps
+constexpr int kRows = 128;               // rows per tile (one block)
+constexpr int kCols = 256;               // columns per tile (two blocks)
+constexpr int kMaxStages = 4;            // row block stages in shared memory
+constexpr int kQueues = 8;               // survivor queues between filter and refine warps
 constexpr int kQueueCap = 256;           // entries per queue
+constexpr int kSlots = kQueueCap / kFilterWarps;   // a filter warp's share of one queue
 constexpr int kMaxKp = 64;               // K up to 64 floats (eight 32-byte panels)
 constexpr long long kWaitCycles = 2000000000ll;   // ~1 s at 2 GHz
 constexpr float kPoisonNorm = 1.2676506002282294e30f;   // 2^100, exact in TF32
 
 struct Args {
-    int n, d, kp, dp, T, b_lo, nb, cap, exact;
-    int diag, delta0, ndelta, npairs, pairs_per_item, items;
-    int row_pad;                 // Npad: first poison row of the B array
-    const float* U;              // filter bounds (Npad + 128)
-    const float* nrm;            // exact fp32 norms (Npad + 128)
-    const uint64_t* thr;         // exact admission thresholds (Npad + 128)
+    int n, d, kp, dp, T, stages, cap, exact;
+    int diag;                    // 1: the diagonal round (X against X)
+    int b_lo, nb;                // row blocks of this shard
+    int r0[2], len[2], np[2];    // forward / backward offset ranges: first offset, length, pairs
+    int ppi, nchunk0, items;     // pairs per work item, items of the forward range, all items
+    const float* V;              // folded filter bounds (precision TF32 rebuilds d2 from them)
+    const float* nrm;            // exact fp32 norms
+    const uint64_t* thr;         // exact admission thresholds
     const float* xp;             // original coordinates, point-major, dp floats per row
-    const unsigned char* aimg;   // A operand: per 128-row block, K/8 pre-swizzled 4 KB panels
-    const unsigned char* bimg;   // B operand, same layout (Npad + 128 rows)
+    const unsigned char* aimg;   // row operand: per 128-row block, K/8 pre-swizzled 4 KB panels
+    const unsigned char* bimg;   // column operand, same layout
     uint64_t* cand;
     int* cnt;
     int* ovf;
@@ -102,8 +114,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity)
 
 // trace-mode phase timers: cycles accumulated per role, added to counters[4 + slot] at the end
 enum {
-    kTProdWaitA, kTProdWaitB, kTMmaWaitA, kTMmaWaitB, kTMmaWaitAcc, kTFiltWait, kTFiltWork, kTRefWait, kTRefWork,
-    kTNum
+    kTProdWaitCols, kTProdWaitRows, kTMmaWaitCols, kTMmaWaitRows, kTMmaWaitAcc, kTFiltWait, kTFiltWork, kTRefWait,
+    kTRefWork, kTNum
 };
 
 // bounded wait: false on timeout or when another role aborted the CTA
@@ -191,83 +203,86 @@ __device__ __forceinline__ void tmem_wait(uint32_t (&r)[32])
                  : "memory");
 }
 
+
 // ------------------------------------------------------------------ shared memory plan
 struct Smem {
     // offsets in bytes from the 1024-aligned base
-    uint32_t a, b[kStages], arow_u, bcol_u[kStages], queue, qcount, bars, misc, total;
+    uint32_t cols, rows[kMaxStages], queue, qcount, bars, misc, total;
 };
 
-__host__ __device__ inline Smem smem_plan(int kp)
+__host__ __device__ inline Smem smem_plan(int kp, int stages)
 {
     Smem s;
     const uint32_t panels = (uint32_t)kp / 8;
     uint32_t o = 0;
-    s.a = o;
-    o += panels * kRows * 32;
-    for (int q = 0; q < kStages; ++q) {
-        s.b[q] = o;
-        o += panels * kCols * 32;
+    s.cols = o;                        // panel p: column block Y (4 KB) then Y + 1 (4 KB)
+    o += panels * kCols * 32;
+    for (int q = 0; q < kMaxStages; ++q) {
+        s.rows[q] = o;
+        if (q < stages) o += panels * kRows * 32;
     }
-    s.arow_u = o;
-    o += kRows * 4;
-    for (int q = 0; q < kStages; ++q) {
-        s.bcol_u[q] = o;
-        o += kCols * 4;
-    }
-    s.queue = o;                       // per queue: rows[cap], first columns[cap], row masks, column masks
-    o += (uint32_t)kQueues * kQueueCap * 16u;
-    s.qcount = o;
-    o += 16 * 4;
+    s.queue = o;                       // per queue: rows[cap], first columns[cap], masks[cap]; filter
+    o += (uint32_t)kQueues * kQueueCap * 12u;   // warp e owns entries [e * kSlots, (e + 1) * kSlots)
+    s.qcount = o;                      // per queue and filter warp: entries written
+    o += kQueues * kFilterWarps * 4;
+    o = (o + 15) & ~15u;
     s.bars = o;
-    o += 24 * 8;
+    o += 32 * 8;
     s.misc = o;
     o += 64;
     s.total = o;
     return s;
 }
 
-// unit (item, index inside item) -> Q block and the two R blocks (-1 = poison half)
-struct Unit {
-    int B, R0, R1;
-};
+// the most row stages (2..4) whose plan fits the 227 KB a CTA may use; 0 if none
+inline int pick_stages(int kp)
+{
+    for (int st = kMaxStages; st >= 2; --st)
+        if (smem_plan(kp, st).total + 1024 <= 227u * 1024u) return st;
+    return 0;
+}
 
-__device__ __forceinline__ int item_units(const Args& a, int item, int& p_lo)
+// ------------------------------------------------------------------ schedule
+// Work item -> (offset range rho, resident column block Y, its pair indices [p_lo, p_lo + count)).
+// Every role walks the same items and tiles in the same order, so tile counters agree.
+__device__ __forceinline__ int item_span(const Args& a, int item, int& rho, int& Y, int& p_lo)
 {
     if (a.diag) {
+        rho = 0;
+        Y = a.b_lo + item;
         p_lo = 0;
         return 1;
     }
-    const int chunk = item / a.nb;
-    p_lo = chunk * a.pairs_per_item;
-    return min(a.npairs, p_lo + a.pairs_per_item) - p_lo;
+    const int gc = item / a.T;
+    Y = item - gc * a.T;
+    rho = gc < a.nchunk0 ? 0 : 1;
+    p_lo = (rho ? gc - a.nchunk0 : gc) * a.ppi;
+    return min(a.np[rho], p_lo + a.ppi) - p_lo;
 }
 
-__device__ __forceinline__ Unit make_unit(const Args& a, int item, int p)
+struct Tile {
+    int X, Y, h1;   // row block, first column block, whether column block Y + 1 belongs to the round
+};
+
+// pair p of an item covers the offsets (delta, delta + 1) = r0 + 2p (+1): rows X = Y - delta;
+// false when X lies outside this shard's row blocks
+__device__ __forceinline__ bool tile_of(const Args& a, int rho, int Y, int p, Tile& t)
 {
-    Unit u;
-    u.B = a.b_lo + item % a.nb;
+    t.Y = Y;
     if (a.diag) {
-        u.R0 = u.B;
-        u.R1 = -1;
-        return u;
+        t.X = Y;
+        t.h1 = 0;
+        return true;
     }
-    int Rs[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int off = 2 * p + h;
-        const int dl = a.delta0 + off;
-        int R = -1;
-        if (off < a.ndelta && !((a.T & 1) == 0 && dl == a.T / 2 && u.B >= a.T / 2)) {
-            R = u.B + dl;
-            if (R >= a.T) R -= a.T;
-        }
-        Rs[h] = R;
-    }
-    u.R0 = Rs[0];
-    u.R1 = Rs[1];
-    return u;
+    const int off = 2 * p;
+    int X = Y - (a.r0[rho] + off);
+    if (X < 0) X += a.T;
+    t.X = X;
+    t.h1 = (off + 1 < a.len[rho]) ? 1 : 0;
+    return (unsigned)(X - a.b_lo) < (unsigned)a.nb;
 }
 
+// ------------------------------------------------------------------ refine and admission
 __device__ __forceinline__ void tc_append(const Args& a, int p, uint64_t key)
 {
     const int slot = atomicAdd(&a.cnt[p], 1);
@@ -285,6 +300,7 @@ __device__ __forceinline__ float refine_global(const Args& a, int gi, int gj)
     const float4* xj4 = reinterpret_cast<const float4*>(xj);
     float dot = 0.0f;
     const int full = a.d >> 2;
+#pragma unroll 4
     for (int c = 0; c < full; ++c) {
         const float4 u = __ldg(xi4 + c), v = __ldg(xj4 + c);
         dot = __fmaf_rn(u.x, v.x, dot);
@@ -296,40 +312,36 @@ __device__ __forceinline__ float refine_global(const Args& a, int gi, int gj)
     return exact_d2(__ldg(a.nrm + gi), __ldg(a.nrm + gj), dot);
 }
 
-// the survivors of one (row gi, 32 columns from gj0): exact refine and admission on both sides
-__device__ __forceinline__ void settle_exact(const Args& a, int gi, int gj0, unsigned mr, unsigned mc)
+// the survivors of row gi among the 32 columns from gj0 (mask m): exact refine and admission
+__device__ __forceinline__ void settle_row(const Args& a, int gi, int gj0, unsigned m)
 {
-    for (unsigned mm = mr | mc; mm; mm &= mm - 1) {
-        const int q = __ffs(mm) - 1;
-        const int gj = gj0 + q;
+    const uint64_t th = __ldg(a.thr + gi);
+    for (; m; m &= m - 1) {
+        const int gj = gj0 + __ffs(m) - 1;
         if (gj == gi || gj >= a.n) continue;
-        const float d2 = refine_global(a, gi, gj);
-        if ((mr >> q) & 1u) {
-            const uint64_t key = pack_key(d2, gj);
-            if (key < __ldg(a.thr + gi)) tc_append(a, gi, key);
-        }
-        if ((mc >> q) & 1u) {
-            const uint64_t key = pack_key(d2, gi);
-            if (key < __ldg(a.thr + gj)) tc_append(a, gj, key);
-        }
+        const uint64_t key = pack_key(refine_global(a, gi, gj), gj);
+        if (key < th) tc_append(a, gi, key);
     }
 }
 
+// ------------------------------------------------------------------ the kernel
 __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    const Smem P = smem_plan(a.kp);
+    const Smem P = smem_plan(a.kp, a.stages);
     const int panels = a.kp / 8;
+    const int S = a.stages;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P.bars);
-    uint64_t* a_full = bars + 0;
-    uint64_t* a_empty = bars + 1;
-    uint64_t* b_full = bars + 2;                     // [kStages]
-    uint64_t* b_empty = b_full + kStages;            // [kStages]
-    uint64_t* acc_full = b_empty + kStages;          // [2]
+    uint64_t* r_full = bars;                         // [kMaxStages] row stage loaded
+    uint64_t* r_empty = r_full + kMaxStages;         // [kMaxStages] row stage consumed by the MMA
+    uint64_t* c_full = r_empty + kMaxStages;         // column pair loaded
+    uint64_t* c_empty = c_full + 1;                  // column pair consumed
+    uint64_t* acc_full = c_empty + 1;                // [2]
     uint64_t* acc_empty = acc_full + 2;              // [2]
     uint64_t* q_full = acc_empty + 2;                // [kQueues]
     uint64_t* q_free = q_full + kQueues;             // [kQueues]
+    uint64_t* drain = q_free + kQueues;              // MMA completion before an early exit
     volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + P.misc);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + P.misc + 16);
     int* qcount = reinterpret_cast<int*>(sm + P.qcount);
@@ -337,12 +349,12 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        mbar_init(a_full, 1);
-        mbar_init(a_empty, kFilterWarps);
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&b_full[s], 1);
-            mbar_init(&b_empty[s], kFilterWarps);
+        for (int s = 0; s < kMaxStages; ++s) {
+            mbar_init(&r_full[s], 1);
+            mbar_init(&r_empty[s], 1);
         }
+        mbar_init(c_full, 1);
+        mbar_init(c_empty, 1);
         for (int s = 0; s < 2; ++s) {
             mbar_init(&acc_full[s], 1);
             mbar_init(&acc_empty[s], kFilterWarps);
@@ -350,8 +362,8 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
         for (int q = 0; q < kQueues; ++q) {
             mbar_init(&q_full[q], kFilterWarps);
             mbar_init(&q_free[q], 1);
-            qcount[q] = 0;
         }
+        mbar_init(drain, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -366,91 +378,120 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const uint32_t a_bytes = (uint32_t)panels * kRows * 32;   // one 128-row block of an image
+    const uint32_t blk_bytes = (uint32_t)panels * kRows * 32;   // one 128-row block of an image
 
     if (warp == 0) {
         // ---------------------------------------------------------------- producer
         if (lane == 0) {
-            int g = 0;
+            int g = 0, ti = 0, c_issued = -1;
             bool ok = true;
             long long tw[2] = {0, 0};
-            for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
-                long long c0 = clock64();
-                if (!mbar_wait(a_empty, (t & 1) ^ 1, abort_flag, a.err, 1)) { ok = false; break; }
-                tw[0] += clock64() - c0;
-                const int B = a.b_lo + item % a.nb;
-                mbar_expect_tx(a_full, a_bytes + kRows * 4);
-                bulk_load(sm + P.a, a.aimg + (size_t)B * a_bytes, a_bytes, a_full);
-                bulk_load(sm + P.arow_u, a.U + (size_t)B * kRows, kRows * 4, a_full);
-                int p_lo;
-                const int nu = item_units(a, item, p_lo);
-                for (int uix = 0; uix < nu; ++uix, ++g) {
-                    const int s = g % kStages;
-                    c0 = clock64();
-                    if (!mbar_wait(&b_empty[s], ((g / kStages) & 1) ^ 1, abort_flag, a.err, 2)) { ok = false; break; }
-                    tw[1] += clock64() - c0;
-                    const Unit u = make_unit(a, item, p_lo + uix);
-                    unsigned char* bb = sm + P.b[s];
-                    mbar_expect_tx(&b_full[s], 2 * a_bytes + 2 * kRows * 4);
-                    const int blk0 = (u.R0 >= 0 ? u.R0 : a.row_pad / kRows);
-                    const int blk1 = (u.R1 >= 0 ? u.R1 : a.row_pad / kRows);
-                    const unsigned char* img0 = a.bimg + (size_t)blk0 * a_bytes;
-                    const unsigned char* img1 = a.bimg + (size_t)blk1 * a_bytes;
-                    for (int p = 0; p < panels; ++p) {
-                        bulk_load(bb + p * kCols * 32, img0 + p * kRows * 32, kRows * 32, &b_full[s]);
-                        bulk_load(bb + p * kCols * 32 + kRows * 32, img1 + p * kRows * 32, kRows * 32, &b_full[s]);
+            for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
+                int rho, Y, p_lo;
+                const int nu = item_span(a, item, rho, Y, p_lo);
+                bool have = false;
+                for (int u = 0; u < nu; ++u) {
+                    Tile t;
+                    if (!tile_of(a, rho, Y, p_lo + u, t)) continue;
+                    long long c0 = clock64();
+                    if (!have) {
+                        if (!mbar_wait(c_empty, (ti & 1) ^ 1, abort_flag, a.err, 1)) { ok = false; break; }
+                        const int Y1 = (Y + 1 < a.T) ? Y + 1 : 0;
+                        const unsigned char* img0 = a.bimg + (size_t)Y * blk_bytes;
+                        const unsigned char* img1 = a.bimg + (size_t)Y1 * blk_bytes;
+                        mbar_expect_tx(c_full, 2 * blk_bytes);
+                        for (int p = 0; p < panels; ++p) {
+                            bulk_load(sm + P.cols + p * kCols * 32, img0 + p * kRows * 32, kRows * 32, c_full);
+                            bulk_load(sm + P.cols + p * kCols * 32 + kRows * 32, img1 + p * kRows * 32, kRows * 32,
+                                      c_full);
+                        }
+                        have = true;
+                        c_issued = ti;
+                        const long long c1 = clock64();
+                        tw[0] += c1 - c0;
+                        c0 = c1;
                     }
-                    bulk_load(sm + P.bcol_u[s], a.U + (size_t)blk0 * kRows, kRows * 4, &b_full[s]);
-                    bulk_load(sm + P.bcol_u[s] + kRows * 4, a.U + (size_t)blk1 * kRows, kRows * 4, &b_full[s]);
+                    const int s = g % S;
+                    if (!mbar_wait(&r_empty[s], ((g / S) & 1) ^ 1, abort_flag, a.err, 2)) { ok = false; break; }
+                    tw[1] += clock64() - c0;
+                    mbar_expect_tx(&r_full[s], blk_bytes);
+                    bulk_load(sm + P.rows[s], a.aimg + (size_t)t.X * blk_bytes, blk_bytes, &r_full[s]);
+                    ++g;
                 }
+                if (have) ++ti;
             }
             if (a.counters) {
-                atomicAdd(&a.counters[4 + kTProdWaitA], (unsigned long long)tw[0]);
-                atomicAdd(&a.counters[4 + kTProdWaitB], (unsigned long long)tw[1]);
+                atomicAdd(&a.counters[4 + kTProdWaitCols], (unsigned long long)tw[0]);
+                atomicAdd(&a.counters[4 + kTProdWaitRows], (unsigned long long)tw[1]);
             }
             // on abort, let the copies already issued land before the CTA exits (bounded)
             if (!ok) {
                 const long long t0 = clock64();
-                for (int q = 0; q < kStages && q < g; ++q) {
+                for (int q = 0; q < S && q < g; ++q) {
                     const int gl = g - 1 - q;
-                    while (!mbar_try_wait(&b_full[gl % kStages], (gl / kStages) & 1) && clock64() - t0 < kWaitCycles) {
+                    while (!mbar_try_wait(&r_full[gl % S], (gl / S) & 1) && clock64() - t0 < kWaitCycles) {
                     }
                 }
+                if (c_issued >= 0)
+                    while (!mbar_try_wait(c_full, c_issued & 1) && clock64() - t0 < kWaitCycles) {
+                    }
             }
         }
         __syncwarp();
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            int g = 0;
+            int g = 0, ti = 0;
             bool ok = true;
             long long tw[3] = {0, 0, 0};
-            for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
-                long long c0 = clock64();
-                if (!mbar_wait(a_full, t & 1, abort_flag, a.err, 3)) { ok = false; break; }
-                tw[0] += clock64() - c0;
-                int p_lo;
-                const int nu = item_units(a, item, p_lo);
-                for (int uix = 0; uix < nu; ++uix, ++g) {
-                    const int s = g % kStages, acc = g & 1;
-                    c0 = clock64();
-                    if (!mbar_wait(&b_full[s], (g / kStages) & 1, abort_flag, a.err, 4)) { ok = false; break; }
+            const uint32_t cbase = su32(sm + P.cols);
+            for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
+                int rho, Y, p_lo;
+                const int nu = item_span(a, item, rho, Y, p_lo);
+                bool have = false;
+                for (int u = 0; u < nu; ++u) {
+                    Tile t;
+                    if (!tile_of(a, rho, Y, p_lo + u, t)) continue;
+                    long long c0 = clock64();
+                    if (!have) {
+                        if (!mbar_wait(c_full, ti & 1, abort_flag, a.err, 3)) { ok = false; break; }
+                        have = true;
+                        const long long c1 = clock64();
+                        tw[0] += c1 - c0;
+                        c0 = c1;
+                    }
+                    const int s = g % S, acc = g & 1;
+                    if (!mbar_wait(&r_full[s], (g / S) & 1, abort_flag, a.err, 4)) { ok = false; break; }
                     const long long c1 = clock64();
                     tw[1] += c1 - c0;
                     if (!mbar_wait(&acc_empty[acc], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 5)) { ok = false; break; }
                     tw[2] += clock64() - c1;
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kCols);
-                    const uint32_t abase = su32(sm + P.a), bbase = su32(sm + P.b[s]);
+                    const uint32_t rbase = su32(sm + P.rows[s]);
                     for (int p = 0; p < panels; ++p)
-                        mma_tf32(d_tmem, sw32_desc(abase + p * kRows * 32), sw32_desc(bbase + p * kCols * 32),
+                        mma_tf32(d_tmem, sw32_desc(rbase + p * kRows * 32), sw32_desc(cbase + p * kCols * 32),
                                  p > 0 ? 1u : 0u);
+                    mma_commit(&r_empty[s]);
                     mma_commit(&acc_full[acc]);
+                    ++g;
+                }
+                if (have && ok) {
+                    mma_commit(c_empty);
+                    ++ti;
+                }
+            }
+            // on abort, wait (bounded) until the MMAs already issued have finished with TMEM
+            if (!ok && g > 0) {
+                mma_commit(drain);
+                const long long t0 = clock64();
+                while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) {
                 }
             }
             if (a.counters) {
-                atomicAdd(&a.counters[4 + kTMmaWaitA], (unsigned long long)tw[0]);
-                atomicAdd(&a.counters[4 + kTMmaWaitB], (unsigned long long)tw[1]);
+                atomicAdd(&a.counters[3], (unsigned long long)g);
+                atomicAdd(&a.counters[4 + kTMmaWaitCols], (unsigned long long)tw[0]);
+                atomicAdd(&a.counters[4 + kTMmaWaitRows], (unsigned long long)tw[1]);
                 atomicAdd(&a.counters[4 + kTMmaWaitAcc], (unsigned long long)tw[2]);
             }
         }
@@ -460,91 +501,82 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
         const int e = warp - 2;                 // 0..7
         const int quad = warp & 3;              // the TMEM lane quarter this warp may read
         const int half = e >> 2;                // column half of the tile
-        const int ra = quad * 32 + lane;        // this thread's A row (tile-local)
+        const int ra = quad * 32 + lane;        // this thread's row in the tile
         int g = 0;
         bool ok = true;
         long long tw[2] = {0, 0};
         unsigned long long inline_entries = 0;
-        for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
-            if (!mbar_wait(a_full, t & 1, abort_flag, a.err, 6)) { ok = false; break; }
-            const float Ui = reinterpret_cast<const float*>(sm + P.arow_u)[ra];
-            int p_lo;
-            const int nu = item_units(a, item, p_lo);
-            for (int uix = 0; uix < nu; ++uix, ++g) {
-                const int s = g % kStages, acc = g & 1, qi = g % kQueues;
+        for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
+            int rho, Y, p_lo;
+            const int nu = item_span(a, item, rho, Y, p_lo);
+            for (int u = 0; u < nu; ++u) {
+                Tile t;
+                if (!tile_of(a, rho, Y, p_lo + u, t)) continue;
+                const int acc = g & 1, qi = g % kQueues;
                 const long long c0 = clock64();
-                if (!mbar_wait(&acc_full[acc], (g >> 1) & 1, abort_flag, a.err, 7)) { ok = false; break; }
-                if (!mbar_wait(&q_free[qi], ((g / kQueues) & 1) ^ 1, abort_flag, a.err, 8)) { ok = false; break; }
+                if (!mbar_wait(&acc_full[acc], (g >> 1) & 1, abort_flag, a.err, 6)) { ok = false; break; }
+                if (!mbar_wait(&q_free[qi], ((g / kQueues) & 1) ^ 1, abort_flag, a.err, 7)) { ok = false; break; }
                 const long long c1 = clock64();
                 tw[0] += c1 - c0;
                 tc_fence_after();
-                const Unit u = make_unit(a, item, p_lo + uix);
-                const int gi = u.B * kRows + ra;
+                const int gi = t.X * kRows + ra;
                 const bool row_real = gi < a.n;
-                const float* cu = reinterpret_cast<const float*>(sm + P.bcol_u[s]);
-                int* qgi = qbase + qi * 4 * kQueueCap;
+                int Yh = t.Y + half;
+                if (Yh >= a.T) Yh -= a.T;
+                int* qgi = qbase + qi * 3 * kQueueCap;
                 int* qgj = qgi + kQueueCap;
-                unsigned* qmr = reinterpret_cast<unsigned*>(qgj + kQueueCap);
-                unsigned* qmc = qmr + kQueueCap;
-                const int rblk = half ? u.R1 : u.R0;
+                unsigned* qm = reinterpret_cast<unsigned*>(qgj + kQueueCap);
+                const float Vi = a.exact ? 0.0f : (row_real ? __ldg(a.V + gi) : 0.0f);
+                const bool inplace = !a.exact && Vi < __int_as_float(0x7f800000);
+                int nq_w = 0;   // entries this warp queued for the tile (warp-uniform)
                 auto process = [&](const uint32_t (&rv)[32], int c) {
-                    const int cb = half * 128 + c * 32;
-                    // four independent partial masks keep the dependency chains short
-                    unsigned mr[4] = {0, 0, 0, 0}, mc[4] = {0, 0, 0, 0};
+                    // a survivor has acc' < 0: OR the raw words and look at the sign bit
+                    uint32_t o8[8];
 #pragma unroll
-                    for (int q = 0; q < 32; q += 4) {
-                        const float4 u4 = *reinterpret_cast<const float4*>(cu + cb + q);
-                        const float uc[4] = {u4.x, u4.y, u4.z, u4.w};
+                    for (int w = 0; w < 8; ++w) o8[w] = (rv[4 * w] | rv[4 * w + 1]) | (rv[4 * w + 2] | rv[4 * w + 3]);
+                    const uint32_t o = ((o8[0] | o8[1]) | (o8[2] | o8[3])) | ((o8[4] | o8[5]) | (o8[6] | o8[7]));
+                    const bool hit = row_real && (int)o < 0;
+                    if (!__any_sync(0xffffffffu, hit)) return;
+                    // survivor mask from the sign bits, four independent chains
+                    unsigned m = 0;
+                    if (hit) {
+                        unsigned p4[4] = {0, 0, 0, 0};
 #pragma unroll
-                        for (int w = 0; w < 4; ++w) {
-                            const float v = __uint_as_float(rv[q + w]);
-                            if (v <= Ui) mr[w] |= 1u << (q + w);
-                            if (v <= uc[w]) mc[w] |= 1u << (q + w);
-                        }
+                        for (int q = 0; q < 32; ++q) p4[q & 3] |= (rv[q] >> 31) << q;
+                        m = (p4[0] | p4[1]) | (p4[2] | p4[3]);
                     }
-                    unsigned mrow = (mr[0] | mr[1]) | (mr[2] | mr[3]);
-                    unsigned mcol = (mc[0] | mc[1]) | (mc[2] | mc[3]);
-                    if (!row_real) mrow = 0;
-                    if (!row_real || a.diag) mcol = 0;   // diagonal tiles: both orders appear as rows
-                    if (!__any_sync(0xffffffffu, (mrow | mcol) != 0u)) return;
-                    const int gj0 = rblk * kRows + c * 32;
-                    if (!a.exact) {
-                        // precision TF32: the accumulator is the distance, admit right here
-                        const unsigned mm = mrow | mcol;
-                        if (mm) {
+                    const int gj0 = Yh * kRows + c * 32;
+                    if (inplace && m) {
+                        // precision TF32 with a finite bound: d2 = acc' + V, admitted right here
+                        const uint64_t th = __ldg(a.thr + gi);
 #pragma unroll
-                            for (int q = 0; q < 32; ++q) {
-                                if (!((mm >> q) & 1u)) continue;
-                                const int gj = gj0 + q;
-                                if (gj == gi || gj >= a.n) continue;
-                                const float d2 = fmaxf(__uint_as_float(rv[q]), 0.0f);
-                                if ((mrow >> q) & 1u) {
-                                    const uint64_t key = pack_key(d2, gj);
-                                    if (key < __ldg(a.thr + gi)) tc_append(a, gi, key);
-                                }
-                                if ((mcol >> q) & 1u) {
-                                    const uint64_t key = pack_key(d2, gi);
-                                    if (key < __ldg(a.thr + gj)) tc_append(a, gj, key);
-                                }
+                        for (int q = 0; q < 32; ++q) {
+                            const int gj = gj0 + q;
+                            if (((m >> q) & 1u) && gj != gi && gj < a.n) {
+                                const uint64_t key = pack_key(fmaxf(__fadd_rn(__uint_as_float(rv[q]), Vi), 0.0f), gj);
+                                if (key < th) tc_append(a, gi, key);
                             }
                         }
-                    } else if (mrow | mcol) {
-                        const int slot = atomicAdd(&qcount[qi], 1);
-                        if (slot < kQueueCap) {
-                            qgi[slot] = gi;
-                            qgj[slot] = gj0;
-                            qmr[slot] = mrow;
-                            qmc[slot] = mcol;
+                    }
+                    // everything else goes to the refine warps through this warp's share of the queue
+                    const unsigned eb = __ballot_sync(0xffffffffu, m != 0u && !inplace);
+                    if (m && !inplace) {
+                        const int slot = nq_w + __popc(eb & ((1u << lane) - 1u));
+                        if (slot < kSlots) {
+                            const int at = e * kSlots + slot;
+                            qgi[at] = gi;
+                            qgj[at] = gj0;
+                            qm[at] = m;
                         } else {
-                            // queue full (dense early rounds): refine in place
-                            settle_exact(a, gi, gj0, mrow, mcol);
+                            // share full (dense early rounds): refine in place
+                            settle_row(a, gi, gj0, m);
                             ++inline_entries;
                         }
                     }
-                    __syncwarp();
+                    nq_w += __popc(eb);
                 };
-                if (rblk >= 0) {
-                    // two chunks in flight: the TMEM load of chunk c + 1 overlaps the filter of chunk c
+                if (half == 0 || t.h1) {
+                    // two chunks in flight: the TMEM load of chunk c + 1 overlaps the test of chunk c
                     const uint32_t tbase =
                         tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * kCols + half * 128);
                     uint32_t r0[32], r1[32];
@@ -561,20 +593,17 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                     tmem_wait(r1);
                     process(r1, 3);
                 }
-                // the accumulator and the B stage are done with: release both, hand the queue over
-                // (the proxy fence orders this warp's reads of the stage before the next bulk copy)
+                // the accumulator is done with: release it and hand the queue over
                 tc_fence_before();
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                if (lane == 0) qcount[qi * kFilterWarps + e] = min(nq_w, kSlots);
                 __syncwarp();
                 tw[1] += clock64() - c1;
                 if (lane == 0) {
                     mbar_arrive(&acc_empty[acc]);
-                    mbar_arrive(&b_empty[s]);
                     mbar_arrive(&q_full[qi]);
                 }
+                ++g;
             }
-            __syncwarp();
-            if (ok && lane == 0) mbar_arrive(a_empty);
         }
         if (a.counters) {
             if (inline_entries) atomicAdd(&a.counters[1], inline_entries);
@@ -590,29 +619,38 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
         bool ok = true;
         long long tw[2] = {0, 0};
         unsigned long long entries = 0;
-        for (int t = 0, item = blockIdx.x; ok && item < a.items; ++t, item += gridDim.x) {
-            int p_lo;
-            const int nu = item_units(a, item, p_lo);
-            for (int uix = 0; uix < nu; ++uix, ++g) {
-                if (g % kRefineWarps != r) continue;
+        for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
+            int rho, Y, p_lo;
+            const int nu = item_span(a, item, rho, Y, p_lo);
+            for (int u = 0; u < nu; ++u) {
+                Tile t;
+                if (!tile_of(a, rho, Y, p_lo + u, t)) continue;
+                const int my = (g % kRefineWarps) == r;
                 const int qi = g % kQueues;
+                ++g;
+                if (!my) continue;
                 const long long c0 = clock64();
-                if (!mbar_wait(&q_full[qi], (g / kQueues) & 1, abort_flag, a.err, 9)) { ok = false; break; }
+                if (!mbar_wait(&q_full[qi], ((g - 1) / kQueues) & 1, abort_flag, a.err, 8)) { ok = false; break; }
                 const long long c1 = clock64();
                 tw[0] += c1 - c0;
-                const int* qgi = qbase + qi * 4 * kQueueCap;
+                const int* qgi = qbase + qi * 3 * kQueueCap;
                 const int* qgj = qgi + kQueueCap;
-                const unsigned* qmr = reinterpret_cast<const unsigned*>(qgj + kQueueCap);
-                const unsigned* qmc = qmr + kQueueCap;
-                const int nq = min(qcount[qi], kQueueCap);
+                const unsigned* qm = reinterpret_cast<const unsigned*>(qgj + kQueueCap);
+                // the filter warps' shares, flattened: entry t of the tile is share e's entry t - start_e
+                const int* cnt_e = qcount + qi * kFilterWarps;
+                int nq = 0;
+#pragma unroll
+                for (int w = 0; w < kFilterWarps; ++w) nq += cnt_e[w];
                 entries += nq;
-                for (int ei = lane; ei < nq; ei += 32) settle_exact(a, qgi[ei], qgj[ei], qmr[ei], qmc[ei]);
+                for (int t = lane; t < nq; t += 32) {
+                    int w = 0, rem = t;
+                    while (rem >= cnt_e[w]) rem -= cnt_e[w++];
+                    const int ei = w * kSlots + rem;
+                    settle_row(a, qgi[ei], qgj[ei], qm[ei]);
+                }
                 __syncwarp();
                 tw[1] += clock64() - c1;
-                if (lane == 0) {
-                    qcount[qi] = 0;
-                    mbar_arrive(&q_free[qi]);
-                }
+                if (lane == 0) mbar_arrive(&q_free[qi]);
                 __syncwarp();
             }
         }
@@ -637,30 +675,13 @@ __device__ __forceinline__ float rna_tf32(float x)
     return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
-__device__ __forceinline__ void split3(float v, float& h, float& m, float& l)
-{
-    h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
-    const float r = __fsub_rn(v, h);
-    m = __uint_as_float(__float_as_uint(r) & 0xFFFFE000u);
-    l = __fsub_rn(r, m);   // at most 2 significant bits remain: exact in TF32
-}
-
-// byte offset of element k of row i inside a blocked, pre-swizzled operand image: 128-row blocks
-// of K/8 panels, each panel 128 rows x 32 bytes with the SWIZZLE_32B chunk order, so one contiguous
-// bulk copy of a panel lands in shared memory exactly as the MMA descriptor expects it
-__device__ __forceinline__ size_t image_offset(int i, int k, int kp)
-{
-    const int blk = i >> 7, r = i & 127, p = k >> 3, c = k & 7;
-    const int phys = ((c >> 2) ^ ((r >> 2) & 1));
-    return (size_t)blk * (kp / 8) * 4096 + (size_t)p * 4096 + (size_t)r * 32 + phys * 16 + (c & 3) * 4;
-}
-
-// One thread per row: TF32-rounded A / B operand rows, the original coordinates point-major (zero
-// padded to dp), and poison for padding rows (their product with any real row is 2^100, above every
-// finite bound).
+// One thread per row: TF32-rounded row (A) and column (B) operand images, the TF32 norm, the
+// original coordinates point-major (zero padded to dp), and poison for padding rows: a padding
+// row's A entry d + 3 and a padding column's B entry d hold 2^100, far above every finite bound.
+// Rows start with the fold of an infinite bound (everything survives until the first merge).
 __global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, int d, int kp, int dp,
                                   int rows_a, int rows_b, unsigned char* __restrict__ A,
-                                  unsigned char* __restrict__ Bm, float* __restrict__ xp)
+                                  unsigned char* __restrict__ Bm, float* __restrict__ xp, float* __restrict__ ntf)
 {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= rows_b) return;
@@ -673,6 +694,7 @@ __global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, i
             put(Bm, k, (k == d) ? kPoisonNorm : 0.0f);
         }
         for (int k = 0; k < dp; ++k) xr[k] = 0.0f;
+        ntf[i] = 0.0f;
         return;
     }
     float nt = 0.0f;
@@ -685,9 +707,10 @@ __global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, i
         xr[k] = xv;
     }
     for (int k = d; k < dp; ++k) xr[k] = 0.0f;
+    ntf[i] = nt;
     float h, m, l;
     split3(nt, h, m, l);
-    const float av[6] = {1.0f, 1.0f, 1.0f, h, m, l};
+    const float av[6] = {1.0f, 1.0f, 1.0f, kFoldAll, 0.0f, 0.0f};
     const float bv[6] = {h, m, l, 1.0f, 1.0f, 1.0f};
     for (int k = d; k < kp; ++k) {
         const int o = k - d;
@@ -702,10 +725,10 @@ __global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, i
 namespace {
 
 struct TcState {
-    int n = 0, d = 0, kp = 0, dp = 0, npad = 0, sms = 0;
+    int n = 0, d = 0, kp = 0, dp = 0, npad = 0, sms = 0, stages = 0;
     unsigned char *A = nullptr, *B = nullptr;
-    float* xp = nullptr;
-    float *U = nullptr, *nrm = nullptr;   // U / nrm / thr belong to the scheduler
+    float *xp = nullptr, *ntf = nullptr;
+    float *V = nullptr, *nrm = nullptr;   // V / nrm / thr belong to the scheduler
     uint64_t* thr = nullptr;
 };
 
@@ -720,13 +743,14 @@ bool tc_engine_supported(int d)
     cudaDeviceProp p;
     if (cudaGetDeviceProperties(&p, dev) != cudaSuccess) return false;
     const int kp = tc_kp(d);
-    return p.major == 10 && p.minor == 0 && kp <= tc::kMaxKp && tc::smem_plan(kp).total + 1024 <= 227 * 1024;
+    return p.major == 10 && p.minor == 0 && kp <= tc::kMaxKp && tc::pick_stages(kp) > 0;
 }
 
-// Prepares the TF32 operand images and the point-major original coordinates for one kNN call; the
-// per-point bounds, norms and thresholds (Npad + 128 entries each) belong to the scheduler.
-void tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const float* norms, const float* U,
-                const uint64_t* thr, cudaStream_t s)
+// Prepares the TF32 operand images, the TF32 norms and the point-major original coordinates for
+// one kNN call; the per-point bounds, norms and thresholds (Npad + 128 entries each) belong to the
+// scheduler, which refreshes the folded bounds in the row image after every merge.
+TcFold tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const float* norms, const float* U,
+                  const uint64_t* thr, cudaStream_t s)
 {
     TcState& st = g_state;
     const int kp = tc_kp(d);
@@ -737,14 +761,16 @@ void tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const floa
     const size_t a_bytes = sizeof(float) * (size_t)npad * kp;
     const size_t b_bytes = sizeof(float) * (size_t)rows_b * kp;
     const size_t x_bytes = sizeof(float) * (size_t)rows_b * dp;
-    char* mem = (char*)ws.ops.ensure(a_bytes + b_bytes + x_bytes + 3072);
+    const size_t n_bytes = sizeof(float) * (size_t)rows_b;
+    char* mem = (char*)ws.ops.ensure(a_bytes + b_bytes + x_bytes + n_bytes + 4096);
     auto align = [](char* p) { return (char*)(((uintptr_t)p + 1023) & ~(uintptr_t)1023); };
     st.A = (unsigned char*)align(mem);
     st.B = (unsigned char*)align((char*)st.A + a_bytes);
     st.xp = (float*)align((char*)st.B + b_bytes);
+    st.ntf = (float*)align((char*)st.xp + x_bytes);
     // the images have no gaps: every element is written by the build kernel
     tc::build_rows_kernel<<<(rows_b + 127) / 128, 128, 0, s>>>(x, ldx, n, d, kp, dp, npad, rows_b, st.A, st.B,
-                                                               st.xp);
+                                                               st.xp, st.ntf);
     FDB_LAUNCHED();
     int dev = 0;
     FDB_CUDA(cudaGetDevice(&dev));
@@ -754,9 +780,14 @@ void tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const floa
     st.kp = kp;
     st.dp = dp;
     st.npad = npad;
-    st.U = const_cast<float*>(U);
+    st.stages = tc::pick_stages(kp);
+    st.V = const_cast<float*>(U);
     st.nrm = const_cast<float*>(norms);
     st.thr = const_cast<uint64_t*>(thr);
+    TcFold f;
+    f.aimg = st.A;
+    f.ntf = st.ntf;
+    return f;
 }
 
 void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStream_t s)
@@ -769,15 +800,13 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.kp = st.kp;
     a.dp = st.dp;
     a.T = r.T;
-    a.b_lo = r.b_lo;
-    a.nb = r.nb;
+    a.stages = st.stages;
     a.cap = r.cap;
     a.exact = precision == FDB200_FP32 ? 1 : 0;
     a.diag = r.diag;
-    a.delta0 = r.delta0;
-    a.ndelta = r.ndelta;
-    a.row_pad = st.npad;
-    a.U = st.U;
+    a.b_lo = r.b_lo;
+    a.nb = r.nb;
+    a.V = st.V;
     a.nrm = st.nrm;
     a.thr = st.thr;
     a.xp = st.xp;
@@ -789,20 +818,29 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.err = r.ovf + 1;
     a.counters = r.counters;
     if (r.diag) {
-        a.npairs = 1;
-        a.pairs_per_item = 1;
         a.items = r.nb;
+        a.ppi = 1;
     } else {
-        a.npairs = (r.ndelta + 1) / 2;
+        // forward offsets [d0, d0 + L) and their mirrors T - delta, the offset T/2 only once
+        const int T = r.T, d0 = r.delta0, L = r.ndelta;
+        const int e = ((T & 1) == 0 && d0 + L - 1 == T / 2) ? 1 : 0;
+        a.r0[0] = d0;
+        a.len[0] = L;
+        a.r0[1] = T - (d0 + L - 1) + e;
+        a.len[1] = L - e;
+        a.np[0] = (a.len[0] + 1) / 2;
+        a.np[1] = (a.len[1] + 1) / 2;
         // about 8 items per CTA so the tail of a round stays short
         const long long want_items = 8ll * st.sms;
-        int ppi = (int)std::max<long long>(1, ((long long)a.npairs * r.nb + want_items - 1) / want_items);
-        ppi = std::min(ppi, a.npairs);
-        a.pairs_per_item = ppi;
-        a.items = r.nb * ((a.npairs + ppi - 1) / ppi);
+        const long long pairs = (long long)T * (a.np[0] + a.np[1]);
+        int ppi = (int)std::max<long long>(1, (pairs + want_items - 1) / want_items);
+        ppi = std::min(ppi, std::max(a.np[0], 1));
+        a.ppi = ppi;
+        a.nchunk0 = (a.np[0] + ppi - 1) / ppi;
+        a.items = T * (a.nchunk0 + (a.np[1] + ppi - 1) / ppi);
     }
-    if (a.items <= 0) return;
-    const tc::Smem P = tc::smem_plan(st.kp);
+    if (a.items <= 0 || r.nb <= 0) return;
+    const tc::Smem P = tc::smem_plan(st.kp, st.stages);
     const size_t smem = P.total + 1024;
     static bool attr_set = false;
     if (!attr_set) {
