@@ -444,6 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
             int g = 0, ti = 0;
             bool ok = true;
             long long tw[3] = {0, 0, 0};
+            const long long t_start = clock64();
             const uint32_t cbase = su32(sm + P.cols);
             for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
                 int rho, Y, p_lo;
@@ -490,6 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
             }
             if (a.counters) {
                 atomicAdd(&a.counters[3], (unsigned long long)g);
+                atomicAdd(&a.counters[15], (unsigned long long)(clock64() - t_start));
                 atomicAdd(&a.counters[4 + kTMmaWaitCols], (unsigned long long)tw[0]);
                 atomicAdd(&a.counters[4 + kTMmaWaitRows], (unsigned long long)tw[1]);
                 atomicAdd(&a.counters[4 + kTMmaWaitAcc], (unsigned long long)tw[2]);
