@@ -34,13 +34,17 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "symwarp-fastdec_b200"))
 
 PUBLISHED_A6000_FIT_S = 16.49          # README.md:149, symwarp FP32 Fit seconds on GloVe 50d (A6000)
+# DRAM traffic of the tile kernels over one fit of the default workload, from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum summed over the nine knn_tile_tc launches of a fit:
+# 589.9 GB read + 20.2 GB written). A one-pass metric set, so it was taken on the full workload.
+TILE_DRAM_BYTES_PER_FIT = 610.03e9
 WORKLOAD = dict(n=1_291_147, d=50, k=45, c=20)
 
 
 def parse():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=3)
+    p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--n", type=int, default=WORKLOAD["n"])
@@ -60,6 +64,10 @@ def parse():
 def dataset(a):
     from fastdec_b200.datasets import embedding_cloud
     return embedding_cloud(n=a.n, d=a.d, seed=a.seed)
+
+
+def engine_name(stats):
+    return {1: "simt", 2: "tcgen05"}.get(stats[-1].get("engine_used") if stats else None, "?")
 
 
 def pairs_of(n):
@@ -322,11 +330,18 @@ def main():
     tf32_peak = bf16 / 2.0
     flops = shard_pairs * 2 * d
     achieved = flops / (tile_ms / 1e3) / 1e12 if tile_ms > 0 else None
-    roofline = {"bound": "tensor", "kernel": "distance tiles (knn_tile_*)",
+    default_shape = (n, d, k, world, a.precision) == (WORKLOAD["n"], WORKLOAD["d"], WORKLOAD["k"], 1, "fp32")
+    kp = ((d + 6 + 7) // 8) * 8
+    roofline = {"bound": "tensor", "kernel": "distance tiles (knn_tile_tc, all rounds of a fit)",
                 "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
-                "frac": (achieved / tf32_peak) if achieved else None, "traffic": None,
-                "peak_note": f"dense TF32 = 1/2 of the {src} bf16 burst figure ({bf16} TF/s)",
-                "launches_per_fit": rounds, "algorithmic_flops_per_fit": flops}
+                "frac": (achieved / tf32_peak) if achieved else None,
+                "traffic": TILE_DRAM_BYTES_PER_FIT if default_shape else None,
+                "traffic_unit": "bytes per fit (ncu, tile kernels)",
+                "peak_note": f"dense TF32 = 1/2 of the {src} bf16 burst figure ({bf16} TF/s); of measured",
+                "launches_per_fit": rounds, "algorithmic_flops_per_fit": flops,
+                "algorithmic_note": "N(N-1)/2 pairs x 2d FLOPs (the reference's -2 X X^T GEMM work)",
+                "tensor_flops_per_fit": float(n) * n * kp * 2 if engine_name(stats) == "tcgen05" else None,
+                "tensor_note": "what the tcgen05 pipe executes: every ordered pair, K = d + 6 padded to 8"}
     last = stats[-1]
     out = {"metric": "fit_distance_pairs_per_s", "value": value, "unit": "pairs/s", "n_gpus": world,
            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -336,7 +351,7 @@ def main():
            "stages_ms": {k2: last.get(k2) for k2 in ("knn_ms", "knn_tile_ms", "density_ms", "dc_ms", "labels_ms")},
            "rounds": last.get("rounds"), "admitted_candidates": last.get("candidates"),
            "num_cores": last.get("num_cores"), "final_k": last.get("final_k"),
-           "engine_used": {1: "simt", 2: "tcgen05"}.get(last.get("engine_used"), "?"),
+           "engine_used": engine_name(stats),
            "centers": centers.cpu().tolist(), "gpu_launches": launches, "clocks": clk.summary(),
            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
            "vs_baseline_note": "value / (8.3353e11 pairs / 16.49 s): the reference's published symwarp FP32 "
