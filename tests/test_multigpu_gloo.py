@@ -1,0 +1,91 @@
+"""Host-side logic of the sharded kNN (fastdec_b200.multigpu) on CPU: two gloo ranks exchange partial
+per-point lists to their owners and gather the merged ranges on rank 0. The k-smallest selection that
+fdb200_merge_lists performs on the GPU is restated here with numpy, so the test checks that the exchange
+delivers every rank's partial list of every point to exactly the owner of that point, and that the
+gathered result equals the k-smallest over all shards (what a single-GPU run computes)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from fastdec_b200.multigpu import exchange_to_owners, gather_to_root, owner_ranges
+
+EMPTY = np.uint64(0xFFFFFFFFFFFFFFFF)
+
+
+def partial_lists(n, k, world, seed):
+    """Packed (d2 bits << 32 | idx) partial lists per shard, sorted, with empty tails."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for s in range(world):
+        keys = np.full((n, k), EMPTY, dtype=np.uint64)
+        for i in range(n):
+            m = int(rng.integers(0, k + 1))
+            d2 = np.sort(rng.random(m).astype(np.float32))
+            idx = rng.integers(0, n, size=m).astype(np.uint64)
+            keys[i, :m] = np.sort((d2.view(np.uint32).astype(np.uint64) << np.uint64(32)) | idx)
+        out.append(keys)
+    return out
+
+
+def k_smallest(blocks, k):
+    cat = np.concatenate(blocks, axis=1)
+    return np.sort(cat, axis=1)[:, :k]
+
+
+def _worker(rank, world, port, n, k, seed, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        parts = partial_lists(n, k, world, seed)
+        mine = torch.from_numpy(parts[rank].view(np.int64).copy())
+        blocks = exchange_to_owners(mine, rank, world)
+        a, b = owner_ranges(n, world)[rank]
+        assert blocks.shape == (world, b - a, k)
+        for s in range(world):
+            assert np.array_equal(blocks[s].numpy().view(np.uint64), parts[s][a:b])
+        merged = torch.from_numpy(k_smallest([blocks[s].numpy().view(np.uint64) for s in range(world)], k)
+                                  .view(np.int64).copy())
+        full = gather_to_root(merged, n, rank, world)
+        if rank == 0:
+            want = k_smallest(parts, k)
+            assert np.array_equal(full.numpy().view(np.uint64), want)
+        q.put((rank, "ok"))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("n,k", [(37, 5), (256, 12), (3, 4)])
+def test_exchange_and_gather_two_ranks(n, k):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, n, k, 7 + n, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert results == {0: "ok", 1: "ok"}
+
+
+def test_owner_ranges_cover_every_point_once():
+    for n in (1, 5, 128, 1_291_147):
+        for world in (1, 2, 3, 8):
+            rng = owner_ranges(n, world)
+            assert rng[0][0] == 0 and rng[-1][1] == n
+            assert all(rng[i][1] == rng[i + 1][0] for i in range(world - 1))
