@@ -168,6 +168,31 @@ int fdb200_fit_from_knn(const float* data, const float* knn_dist_dev, const int*
 /* Frees the library's cached device workspace on opts->device. */
 int fdb200_release(const FdB200Opts* opts);
 
+/*
+ * fdb200_density without any allocation. No counterpart in the reference (every reference call,
+ * and every other entry point here, obtains device memory as it goes). It is for callers that must
+ * not allocate while they run: a serving loop that reserved all device memory up front, a process
+ * whose memory belongs to another framework's caching allocator, or code that cannot afford the
+ * device-wide synchronisation and the out-of-memory failure point that cudaMalloc / cudaFree bring.
+ *
+ * Same densities and mean as fdb200_density (Laplacian or Gaussian per opts->density_kernel), from
+ * DEVICE pointers on opts->device: knn_dist_dev rank-major (rank stride n, k ranks),
+ * densities_dev n floats, mean_dev one double. The working memory is a fixed array inside the
+ * library image, sized for at most FDB200_NOALLOC_MAX_POINTS points; a larger n returns
+ * FDB200_EINVAL without launching anything. Nothing in that array needs to start at zero: each call
+ * writes every word it later reads.
+ *
+ * Asynchronous on opts->stream (NULL = the legacy default stream); results are ready when the
+ * stream reaches them. The array is shared by all calls on a device, so calls whose executions
+ * overlap (two streams, or two host threads with no ordering between them) race and corrupt each
+ * other's mean: order them on one stream or with events. The first call on each device looks up
+ * the array's address (cudaGetSymbolAddress, which may load the module); make that first call
+ * before any stream capture begins.
+ */
+#define FDB200_NOALLOC_MAX_POINTS 4194304
+int fdb200_density_noalloc(const float* knn_dist_dev, int n, int k, const FdB200Opts* opts,
+                           float* densities_dev, double* mean_dev);
+
 #ifdef __cplusplus
 }
 #endif

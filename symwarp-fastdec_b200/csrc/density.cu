@@ -325,6 +325,53 @@ void exact_mean(Workspace& ws, const float* dist, int n, int k, double* mean_dev
     FDB_LAUNCHED();
 }
 
+static_assert(sizeof(BinadeMap) == 32, "mean_scratch_bytes assumes 32-byte maps");
+
+// exact_mean with caller-supplied scratch laid out as mean_scratch_bytes describes; every word the
+// kernels read is written earlier in the same call, so the scratch needs no initial contents
+void exact_mean_in(void* scratch, size_t scratch_bytes, const float* dist, int n, int k, double* mean_dev,
+                   cudaStream_t s)
+{
+    FDB_REQUIRE(scratch_bytes >= mean_scratch_bytes(n), "mean scratch too small for " + std::to_string(n) +
+                                                            " points");
+    const int nchunks = (n + 31) / 32;
+    int counts[kLevels];
+    int nlev = 0;
+    int c = nchunks;
+    counts[nlev++] = c;
+    while (c > 1 && nlev < kLevels) {
+        c = (c + 31) / 32;
+        counts[nlev++] = c;
+    }
+    FDB_REQUIRE(counts[nlev - 1] <= 32 * 32, "too many points for the mean tree");
+    double* csum = (double*)scratch;
+    double* pre = csum + nchunks;
+    BinadeMap* maps = (BinadeMap*)(((uintptr_t)(pre + nchunks) + 15) & ~uintptr_t(15));
+    MeanLevels L;
+    L.nlev = nlev;
+    BinadeMap* cur = maps;
+    for (int l = 0; l < nlev; ++l) {
+        L.lvl[l] = cur;
+        L.count[l] = counts[l];
+        cur += counts[l];
+    }
+    const int wpb = 8;
+    chunk_sums_kernel<<<(nchunks + wpb - 1) / wpb, wpb * 32, 0, s>>>(dist, n, k, csum, nchunks);
+    FDB_LAUNCHED();
+    prefix_kernel<<<1, 1024, 0, s>>>(csum, nchunks, pre);
+    FDB_LAUNCHED();
+    chunk_maps_kernel<<<(nchunks + wpb - 1) / wpb, wpb * 32, 0, s>>>(dist, n, k, pre, csum,
+                                                                     (BinadeMap*)L.lvl[0], nchunks);
+    FDB_LAUNCHED();
+    for (int l = 1; l < nlev; ++l) {
+        compose_level_kernel<<<(counts[l] + wpb - 1) / wpb, wpb * 32, 0, s>>>(
+            L.lvl[l - 1], counts[l - 1], (BinadeMap*)L.lvl[l], counts[l]);
+        FDB_LAUNCHED();
+    }
+    resolve_mean_kernel<<<1, 32, 0, s>>>(L, dist, n, k, mean_dev);
+    FDB_LAUNCHED();
+}
+
 void density_from_mean(const float* dist, int n, int k, int gaussian, const double* mean_dev, float* den,
                        cudaStream_t s)
 {

@@ -129,6 +129,21 @@ TcFold tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const fl
 // Sequential-order double mean of the first k ranks (rank stride n) -- bit-identical to the
 // host loop fastdecbase.cpp:257-274. Result left in *mean_dev.
 void exact_mean(Workspace& ws, const float* dist_rm, int n, int k, double* mean_dev, cudaStream_t s);
+// The same mean with its working memory supplied by the caller (no workspace, no allocation).
+// mean_scratch_bytes(n) is the space it needs: two doubles per 32-point chunk plus the binade-map
+// tree (32 bytes per map, one level per factor of 32).
+constexpr size_t mean_scratch_bytes(long long n)
+{
+    const long long nchunks = (n + 31) / 32;
+    long long maps = nchunks, c = nchunks;
+    while (c > 1) {
+        c = (c + 31) / 32;
+        maps += c;
+    }
+    return (size_t)(16 * nchunks + 16 + 32 * maps + 256);
+}
+void exact_mean_in(void* scratch, size_t scratch_bytes, const float* dist_rm, int n, int k, double* mean_dev,
+                   cudaStream_t s);
 void density_from_mean(const float* dist_rm, int n, int k, int gaussian, const double* mean_dev,
                        float* den, cudaStream_t s);
 // parent + ordered core list; returns the core count (synchronises on s)

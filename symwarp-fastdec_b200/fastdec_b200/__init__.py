@@ -63,7 +63,7 @@ class Stats(ctypes.Structure):
 EXPORTS = ["fdb200_opts_init", "fdb200_last_error", "fdb200_abi_version", "fdb200_knn", "fdb200_fit",
            "fdb200_dc_reduction", "fdb200_density", "fdb200_dc_detection", "fdb200_final_cluster",
            "fdb200_knn_partial", "fdb200_merge_lists", "fdb200_lists_to_knn", "fdb200_fit_from_knn",
-           "fdb200_release"]
+           "fdb200_release", "fdb200_density_noalloc"]
 
 _lib = None
 
