@@ -66,6 +66,15 @@ def dataset(a):
     return embedding_cloud(n=a.n, d=a.d, seed=a.seed)
 
 
+_T0 = time.time()
+
+
+def progress(*msg):
+    """one stderr line per phase when FASTDEC_BENCH_LOG=1 (rank and seconds since start)"""
+    if os.environ.get("FASTDEC_BENCH_LOG") == "1":
+        print(f"[rank {os.environ.get('RANK', '0')} {time.time() - _T0:8.2f}s]", *msg, file=sys.stderr, flush=True)
+
+
 def engine_name(stats):
     return {1: "simt", 2: "tcgen05"}.get(stats[-1].get("engine_used") if stats else None, "?")
 
@@ -220,13 +229,17 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        # the exchange is an all-to-all and a gather: in-switch reduction (NVLS) brings nothing here
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
     fdb.lib()
 
+    progress("process group ready")
     x_host = dataset(a)
     n, d, k, c = a.n, a.d, a.k, a.c
+    progress("dataset ready")
     x_dev = torch.from_numpy(x_host).to(dev)
     centers = torch.empty(c, dtype=torch.int32, device=dev)
     labels = torch.empty(n, dtype=torch.int32, device=dev)
@@ -242,8 +255,9 @@ def main():
         def step():
             return fdb.fit_device(x_dev, k, c, centers, labels, stream=sp, **kw)
 
-    for _ in range(a.warmup):
+    for w in range(a.warmup):
         st = step()
+        progress("warm-up step", w)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
@@ -262,6 +276,7 @@ def main():
         if world > 1:
             dist.barrier()
     ms = ev0.elapsed_time(ev1)
+    progress("timed steps done", ms)
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -306,6 +321,7 @@ def main():
         e1.record(stream)
         torch.cuda.synchronize(dev)
         ems = e0.elapsed_time(e1)
+        progress("e2e steps done", ems)
         if world > 1:
             t = torch.tensor([ems], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)

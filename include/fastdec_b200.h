@@ -51,7 +51,8 @@ typedef struct FdB200Opts {
     int shard_rank;           /* kNN triangle sharding: this shard's index ... */
     int shard_count;          /* ... out of shard_count (1 = whole triangle) */
     int cand_capacity;        /* per-point candidate slots per round (0 = automatic) */
-    void* stream;             /* cudaStream_t to run on; NULL = the library's own stream */
+    void* stream;             /* cudaStream_t to run on; NULL = the library's own stream (pass
+                                 cudaStreamLegacy to run on the legacy default stream) */
 } FdB200Opts;
 
 typedef struct FdB200Stats {

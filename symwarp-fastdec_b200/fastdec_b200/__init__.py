@@ -100,6 +100,9 @@ def lib():
     return _lib
 
 
+_CUDA_STREAM_LEGACY = 0x1   # cudaStreamLegacy
+
+
 def make_opts(device=0, precision="fp32", density="laplacian", engine="auto", on_device=False,
               shard=(0, 1), cand_capacity=0, stream=None):
     o = Opts()
@@ -111,7 +114,13 @@ def make_opts(device=0, precision="fp32", density="laplacian", engine="auto", on
     o.inputs_on_device = o.outputs_on_device = int(bool(on_device))
     o.shard_rank, o.shard_count = int(shard[0]), int(shard[1])
     o.cand_capacity = int(cand_capacity)
-    o.stream = stream
+    # stream: None = the library's own stream; an integer handle runs the call on that CUDA stream.
+    # Handle 0 is the legacy default stream (torch's default stream reports 0); the ABI reserves a
+    # NULL stream for "the library's own", so it is passed as cudaStreamLegacy.
+    if stream is None:
+        o.stream = None
+    else:
+        o.stream = _CUDA_STREAM_LEGACY if int(stream) == 0 else int(stream)
     return o
 
 

@@ -13,8 +13,18 @@ the same code runs over NCCL on B200s and over gloo on CPU tensors in the tests.
 """
 from __future__ import annotations
 
+import os
+import sys
+import time
+
 import torch
 import torch.distributed as dist
+
+
+def _log(rank, *msg):
+    """per-phase stderr line when FASTDEC_BENCH_LOG=1"""
+    if os.environ.get("FASTDEC_BENCH_LOG") == "1":
+        print(f"[rank {rank} {time.time():.3f}]", *msg, file=sys.stderr, flush=True)
 
 
 def owner_ranges(n: int, world: int):
@@ -36,21 +46,21 @@ def exchange_to_owners(lists: torch.Tensor, rank: int, world: int) -> torch.Tens
 
 
 def gather_to_root(merged: torch.Tensor, n: int, rank: int, world: int):
-    """merged: (n_own, k) final lists of this rank's points. Rank 0 receives the full (n, k)."""
+    """merged: (n_own, k) final lists of this rank's points. Rank 0 receives the full (n, k).
+
+    A collective (all-gather of equal, padded blocks) rather than point-to-point sends: collectives on
+    one communicator run in the same order on every rank, so a rank that has already moved on to
+    the next step's kernels cannot hold back the transfer that rank 0 is waiting for."""
     k = merged.shape[1]
     rng = owner_ranges(n, world)
-    if rank == 0:
-        full = torch.empty((n, k), dtype=merged.dtype, device=merged.device)
-        full[rng[0][0]:rng[0][1]].copy_(merged)
-        ops = [dist.P2POp(dist.irecv, full[a:b], s) for s, (a, b) in enumerate(rng) if s != 0 and b > a]
-        if ops:
-            for req in dist.batch_isend_irecv(ops):
-                req.wait()
-        return full
-    if merged.shape[0] > 0:
-        for req in dist.batch_isend_irecv([dist.P2POp(dist.isend, merged.contiguous(), 0)]):
-            req.wait()
-    return None
+    width = max(b - a for a, b in rng)
+    pad = torch.empty((width, k), dtype=merged.dtype, device=merged.device)
+    pad[:merged.shape[0]].copy_(merged)
+    parts = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(parts, pad)
+    if rank != 0:
+        return None
+    return torch.cat([parts[s][:b - a] for s, (a, b) in enumerate(rng)], dim=0)
 
 
 class ShardedFit:
@@ -69,13 +79,18 @@ class ShardedFit:
 
     def step(self, x_dev, centers, labels):
         fdb, n, k = self.fdb, self.n, self.k
+        _log(self.rank, "step: partial kNN")
         st = fdb.knn_partial_device(x_dev, k, self.lists, (self.rank, self.world), stream=self.sp, **self.opts)
+        _log(self.rank, "step: exchange", st.get("knn_ms"))
         blocks = exchange_to_owners(self.lists, self.rank, self.world)
         n_own = blocks.shape[1]
+        _log(self.rank, "step: merge")
         if n_own > 0:
             fdb.merge_lists_device(blocks[0], blocks[1:], self.world - 1, n_own, k, stream=self.sp,
                                    device=self.dev.index or 0)
+        _log(self.rank, "step: gather")
         full = gather_to_root(blocks[0], n, self.rank, self.world)
+        _log(self.rank, "step: tail")
         if self.rank == 0:
             fdb.lists_to_knn_device(full, n, k, self.dist, self.idx, stream=self.sp, device=self.dev.index or 0)
             tail = fdb.fit_from_knn_device(x_dev, self.dist, self.idx, k, self.c, centers, labels, stream=self.sp,
@@ -85,6 +100,7 @@ class ShardedFit:
             st["launches"] = st.get("launches", 0) + tail.get("launches", 0) + 1   # + lists_to_knn
         if n_own > 0:
             st["launches"] = st.get("launches", 0) + 1                              # + merge
+        _log(self.rank, "step: done")
         return st
 
     def close(self):
