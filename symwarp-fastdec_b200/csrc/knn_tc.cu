@@ -18,7 +18,8 @@
 //      instruction per pair.
 //   3. Exact refine. A survivor is recomputed with the sequential fmaf chain on the ORIGINAL FP32
 //      coordinates (a point-major copy in global memory) and admitted with the exact lexicographic
-//      test. Precision TF32 keeps d2 = max(acc' + V_i, 0) instead.
+//      test. Precision TF32 folds the plain threshold (no margin), so near-threshold candidates may
+//      be missed; the distances it does admit are still exact.
 //
 // Schedule: the engine visits ORDERED block pairs and tests rows only. A round with offsets
 // [a, a + L) covers, for every row block X, the column blocks X + delta and X - delta (mod T) for
@@ -34,10 +35,12 @@
 //   warp 1       TMEM owner and MMA issuer (one thread): K/8 tcgen05.mma kind::tf32 per tile into
 //                one of two 256-column TMEM accumulators; tcgen05.commit frees the row stage and
 //                publishes the accumulator
-//   warps 2..9   filter: tcgen05.ld 32 columns at a time (two loads in flight), sign-bit test,
-//                survivor masks into a per-tile queue; then the accumulator is released
-//   warps 10..15 refine: warp r owns the tiles g = r mod 6 and drains their queues (exact refine
-//                from global memory, admission, append), off the filter's critical path
+//   warps 2..9   filter: tcgen05.ld 32 columns at a time (two loads in flight), sign-bit test; a
+//                row with survivors parks its 32 accumulator words in shared memory and queues
+//                itself; then the accumulator is released
+//   warps 10..15 refine: warp r owns the tiles g = r mod 6 and drains their queues (survivor masks
+//                from the parked words, exact refine from global memory, admission, append), off
+//                the filter's critical path
 // Every mbarrier wait is bounded (about a second); on a timeout the CTA records an error code,
 // stops issuing work, frees its TMEM and returns, and the host reports the failure.
 #include "knn_common.cuh"
@@ -59,6 +62,7 @@ constexpr int kMaxStages = 4;            // row block stages in shared memory
 constexpr int kQueues = 8;               // survivor queues between filter and refine warps
 constexpr int kQueueCap = 256;           // entries per queue
 constexpr int kSlots = kQueueCap / kFilterWarps;   // a filter warp's share of one queue
+constexpr int kRawPerWarp = 4;           // survivor rows a filter warp may park raw per tile
 constexpr int kMaxKp = 64;               // K up to 64 floats (eight 32-byte panels)
 constexpr long long kWaitCycles = 2000000000ll;   // ~1 s at 2 GHz
 constexpr float kPoisonNorm = 1.2676506002282294e30f;   // 2^100, exact in TF32
@@ -69,7 +73,7 @@ struct Args {
     int b_lo, nb;                // row blocks of this shard
     int r0[2], len[2], np[2];    // forward / backward offset ranges: first offset, length, pairs
     int ppi, nchunk0, items;     // pairs per work item, items of the forward range, all items
-    const float* V;              // folded filter bounds (precision TF32 rebuilds d2 from them)
+    const float* V;              // folded filter bounds
     const float* nrm;            // exact fp32 norms
     const uint64_t* thr;         // exact admission thresholds
     const float* xp;             // original coordinates, point-major, dp floats per row
@@ -207,7 +211,7 @@ __device__ __forceinline__ void tmem_wait(uint32_t (&r)[32])
 // ------------------------------------------------------------------ shared memory plan
 struct Smem {
     // offsets in bytes from the 1024-aligned base
-    uint32_t cols, rows[kMaxStages], queue, qcount, bars, misc, total;
+    uint32_t cols, rows[kMaxStages], queue, qcount, raw, bars, misc, total;
 };
 
 __host__ __device__ inline Smem smem_plan(int kp, int stages)
@@ -226,6 +230,8 @@ __host__ __device__ inline Smem smem_plan(int kp, int stages)
     s.qcount = o;                      // per queue and filter warp: entries written
     o += kQueues * kFilterWarps * 4;
     o = (o + 15) & ~15u;
+    s.raw = o;                         // per queue and filter warp: kRawPerWarp rows of 32 words
+    o += (uint32_t)kQueues * kFilterWarps * kRawPerWarp * 128u;
     s.bars = o;
     o += 32 * 8;
     s.misc = o;
@@ -528,9 +534,9 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                 int* qgi = qbase + qi * 3 * kQueueCap;
                 int* qgj = qgi + kQueueCap;
                 unsigned* qm = reinterpret_cast<unsigned*>(qgj + kQueueCap);
-                const float Vi = a.exact ? 0.0f : (row_real ? __ldg(a.V + gi) : 0.0f);
-                const bool inplace = !a.exact && Vi < __int_as_float(0x7f800000);
                 int nq_w = 0;   // entries this warp queued for the tile (warp-uniform)
+                int raw_w = 0;  // survivor rows this warp parked raw for the tile (warp-uniform)
+                uint32_t* rawq = reinterpret_cast<uint32_t*>(sm + P.raw) + qi * kFilterWarps * kRawPerWarp * 32;
                 auto process = [&](const uint32_t (&rv)[32], int c) {
                     // a survivor has acc' < 0: OR the raw words and look at the sign bit
                     uint32_t o8[8];
@@ -539,43 +545,43 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                     const uint32_t o = ((o8[0] | o8[1]) | (o8[2] | o8[3])) | ((o8[4] | o8[5]) | (o8[6] | o8[7]));
                     const bool hit = row_real && (int)o < 0;
                     if (!__any_sync(0xffffffffu, hit)) return;
-                    // survivor mask from the sign bits, four independent chains
-                    unsigned m = 0;
-                    if (hit) {
-                        unsigned p4[4] = {0, 0, 0, 0};
-#pragma unroll
-                        for (int q = 0; q < 32; ++q) p4[q & 3] |= (rv[q] >> 31) << q;
-                        m = (p4[0] | p4[1]) | (p4[2] | p4[3]);
-                    }
                     const int gj0 = Yh * kRows + c * 32;
-                    if (inplace && m) {
-                        // precision TF32 with a finite bound: d2 = acc' + V, admitted right here
-                        const uint64_t th = __ldg(a.thr + gi);
+                    // A hitting row parks its 32 accumulator words in shared memory (eight 16-byte
+                    // stores) and the refine warp derives the survivor mask from their sign bits; the
+                    // low bits of the queued first column (a multiple of 32) carry the parked slot + 1.
+                    // Only when this warp's parked rows or queue share run out is the mask built here.
+                    const unsigned hb = __ballot_sync(0xffffffffu, hit);
+                    const int before = __popc(hb & ((1u << lane) - 1u));
+                    const int rslot = raw_w + before, slot = nq_w + before;
+                    if (hit) {
+                        if (rslot < kRawPerWarp && slot < kSlots) {
+                            uint4* dst = reinterpret_cast<uint4*>(rawq + (e * kRawPerWarp + rslot) * 32);
 #pragma unroll
-                        for (int q = 0; q < 32; ++q) {
-                            const int gj = gj0 + q;
-                            if (((m >> q) & 1u) && gj != gi && gj < a.n) {
-                                const uint64_t key = pack_key(fmaxf(__fadd_rn(__uint_as_float(rv[q]), Vi), 0.0f), gj);
-                                if (key < th) tc_append(a, gi, key);
+                            for (int w = 0; w < 8; ++w)
+                                dst[w] = make_uint4(rv[4 * w], rv[4 * w + 1], rv[4 * w + 2], rv[4 * w + 3]);
+                            const int at = e * kSlots + slot;
+                            qgi[at] = gi;
+                            qgj[at] = gj0 | (rslot + 1);
+                            qm[at] = 0u;
+                        } else {
+                            unsigned p4[4] = {0, 0, 0, 0};
+#pragma unroll
+                            for (int q = 0; q < 32; ++q) p4[q & 3] |= (rv[q] >> 31) << q;
+                            const unsigned m = (p4[0] | p4[1]) | (p4[2] | p4[3]);
+                            if (slot < kSlots) {
+                                const int at = e * kSlots + slot;
+                                qgi[at] = gi;
+                                qgj[at] = gj0;
+                                qm[at] = m;
+                            } else {
+                                // share full (dense early rounds): refine in place
+                                settle_row(a, gi, gj0, m);
+                                ++inline_entries;
                             }
                         }
                     }
-                    // everything else goes to the refine warps through this warp's share of the queue
-                    const unsigned eb = __ballot_sync(0xffffffffu, m != 0u && !inplace);
-                    if (m && !inplace) {
-                        const int slot = nq_w + __popc(eb & ((1u << lane) - 1u));
-                        if (slot < kSlots) {
-                            const int at = e * kSlots + slot;
-                            qgi[at] = gi;
-                            qgj[at] = gj0;
-                            qm[at] = m;
-                        } else {
-                            // share full (dense early rounds): refine in place
-                            settle_row(a, gi, gj0, m);
-                            ++inline_entries;
-                        }
-                    }
-                    nq_w += __popc(eb);
+                    raw_w += __popc(hb);
+                    nq_w += __popc(hb);
                 };
                 if (half == 0 || t.h1) {
                     // two chunks in flight: the TMEM load of chunk c + 1 overlaps the test of chunk c
@@ -640,6 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                 const unsigned* qm = reinterpret_cast<const unsigned*>(qgj + kQueueCap);
                 // the filter warps' shares, flattened: entry t of the tile is share e's entry t - start_e
                 const int* cnt_e = qcount + qi * kFilterWarps;
+                const uint32_t* rawq = reinterpret_cast<const uint32_t*>(sm + P.raw) + qi * kFilterWarps * kRawPerWarp * 32;
                 int nq = 0;
 #pragma unroll
                 for (int w = 0; w < kFilterWarps; ++w) nq += cnt_e[w];
@@ -648,7 +655,19 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                     int w = 0, rem = t;
                     while (rem >= cnt_e[w]) rem -= cnt_e[w++];
                     const int ei = w * kSlots + rem;
-                    settle_row(a, qgi[ei], qgj[ei], qm[ei]);
+                    const int gq = qgj[ei];
+                    unsigned m = qm[ei];
+                    if (gq & 31) {
+                        // parked row: the survivors are the columns whose accumulator word is negative
+                        const uint4* src = reinterpret_cast<const uint4*>(rawq + (w * kRawPerWarp + (gq & 31) - 1) * 32);
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) {
+                            const uint4 u = src[v];
+                            m |= ((u.x >> 31) << (4 * v)) | ((u.y >> 31) << (4 * v + 1)) | ((u.z >> 31) << (4 * v + 2)) |
+                                 ((u.w >> 31) << (4 * v + 3));
+                        }
+                    }
+                    settle_row(a, qgi[ei], gq & ~31, m);
                 }
                 __syncwarp();
                 tw[1] += clock64() - c1;
