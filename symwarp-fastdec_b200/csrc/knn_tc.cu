@@ -138,6 +138,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile
     return true;
 }
 
+// the same wait with a first test that costs no clock read: most waits of the MMA issuer find the
+// phase already complete, and every cycle that thread spends between tiles is idle tensor pipe
+__device__ __forceinline__ bool mbar_wait_fast(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err,
+                                               int code)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    return ok ? true : mbar_wait(b, parity, abort_flag, err, code);
+}
+
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
 {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -446,12 +462,17 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
         __syncwarp();
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
+        // tcgen05.mma issue stalls once the tensor pipe's short queue is full, so this thread's work
+        // between two tiles is idle pipe time: stages and phases are counters, descriptors are
+        // stepped rather than rebuilt, and a ready barrier costs one test.
         if (lane == 0) {
-            int g = 0, ti = 0;
+            int g = 0, ti = 0, s = 0;
+            uint32_t rph = 0;   // parity of the next row-stage fill
             bool ok = true;
-            long long tw[3] = {0, 0, 0};
             const long long t_start = clock64();
-            const uint32_t cbase = su32(sm + P.cols);
+            const uint64_t cdesc = sw32_desc(su32(sm + P.cols));
+            const uint64_t rdesc0 = sw32_desc(su32(sm + P.rows[0]));
+            const uint64_t rstride = (uint64_t)(blk_bytes >> 4);   // one row stage in descriptor units
             for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
                 int rho, Y, p_lo;
                 const int nu = item_span(a, item, rho, Y, p_lo);
@@ -459,29 +480,26 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                 for (int u = 0; u < nu; ++u) {
                     Tile t;
                     if (!tile_of(a, rho, Y, p_lo + u, t)) continue;
-                    long long c0 = clock64();
                     if (!have) {
-                        if (!mbar_wait(c_full, ti & 1, abort_flag, a.err, 3)) { ok = false; break; }
+                        if (!mbar_wait_fast(c_full, ti & 1, abort_flag, a.err, 3)) { ok = false; break; }
                         have = true;
-                        const long long c1 = clock64();
-                        tw[0] += c1 - c0;
-                        c0 = c1;
                     }
-                    const int s = g % S, acc = g & 1;
-                    if (!mbar_wait(&r_full[s], (g / S) & 1, abort_flag, a.err, 4)) { ok = false; break; }
-                    const long long c1 = clock64();
-                    tw[1] += c1 - c0;
-                    if (!mbar_wait(&acc_empty[acc], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 5)) { ok = false; break; }
-                    tw[2] += clock64() - c1;
+                    const int acc = g & 1;
+                    if (!mbar_wait_fast(&r_full[s], rph, abort_flag, a.err, 4)) { ok = false; break; }
+                    if (!mbar_wait_fast(&acc_empty[acc], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 5)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kCols);
-                    const uint32_t rbase = su32(sm + P.rows[s]);
+                    const uint64_t ad = rdesc0 + (uint64_t)s * rstride;
                     for (int p = 0; p < panels; ++p)
-                        mma_tf32(d_tmem, sw32_desc(rbase + p * kRows * 32), sw32_desc(cbase + p * kCols * 32),
+                        mma_tf32(d_tmem, ad + (uint64_t)(p * ((kRows * 32) >> 4)), cdesc + (uint64_t)(p * ((kCols * 32) >> 4)),
                                  p > 0 ? 1u : 0u);
                     mma_commit(&r_empty[s]);
                     mma_commit(&acc_full[acc]);
                     ++g;
+                    if (++s == S) {
+                        s = 0;
+                        rph ^= 1;
+                    }
                 }
                 if (have && ok) {
                     mma_commit(c_empty);
@@ -498,9 +516,6 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
             if (a.counters) {
                 atomicAdd(&a.counters[3], (unsigned long long)g);
                 atomicAdd(&a.counters[15], (unsigned long long)(clock64() - t_start));
-                atomicAdd(&a.counters[4 + kTMmaWaitCols], (unsigned long long)tw[0]);
-                atomicAdd(&a.counters[4 + kTMmaWaitRows], (unsigned long long)tw[1]);
-                atomicAdd(&a.counters[4 + kTMmaWaitAcc], (unsigned long long)tw[2]);
             }
         }
         __syncwarp();
