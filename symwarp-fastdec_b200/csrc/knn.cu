@@ -221,6 +221,126 @@ __global__ void knn_merge_kernel(uint64_t* __restrict__ lists, uint64_t* __restr
     }
 }
 
+// ---- the same merge without sorting the list: the candidates are sorted in registers (a bitonic
+// network over 32*E keys, blocked layout: key e of lane l sits at position l*E + e; in-lane steps swap
+// registers, cross-lane steps exchange with shfl_xor), then each output rank r < k is placed by a
+// merge-path search over (list, sorted candidates) in shared memory. Shared memory is touched only
+// to stage the two sorted runs, so the shared-memory traffic that bounds the sorting version goes.
+template <int E>
+__device__ __forceinline__ void warp_sort_regs(uint64_t (&v)[E], int lane)
+{
+    constexpr int m = 32 * E;
+#pragma unroll
+    for (int size = 2; size <= m; size <<= 1) {
+#pragma unroll
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            if (j < E) {
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    const int e2 = e ^ j;
+                    if (e2 > e) {
+                        const bool asc = ((lane * E + e) & size) == 0;
+                        const uint64_t a = v[e], b = v[e2];
+                        if ((a > b) == asc) {
+                            v[e] = b;
+                            v[e2] = a;
+                        }
+                    }
+                }
+            } else {
+                const int lx = j / E;
+                const bool lower = (lane & lx) == 0;
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    const uint64_t o = __shfl_xor_sync(0xffffffffu, v[e], lx);
+                    const bool asc = ((lane * E + e) & size) == 0;
+                    const bool take_min = (lower == asc);
+                    const uint64_t mn = v[e] < o ? v[e] : o, mx = v[e] < o ? o : v[e];
+                    v[e] = take_min ? mn : mx;
+                }
+            }
+        }
+    }
+}
+
+// number of list keys among the first r outputs of merge(list, cand), list first on ties
+__device__ __forceinline__ int merge_split(const uint64_t* L, int nl, const uint64_t* C, int nc, int r)
+{
+    int lo = max(0, r - nc), hi = min(r, nl);
+    while (lo < hi) {
+        const int i = (lo + hi + 1) >> 1;   // try taking i list keys: needs L[i-1] <= C[r-i]
+        if (L[i - 1] <= C[r - i]) lo = i;
+        else hi = i - 1;
+    }
+    return lo;
+}
+
+template <int E>
+__device__ __forceinline__ void merge_point_sorted(uint64_t* __restrict__ lists, const uint64_t* __restrict__ cp,
+                                                   int c, int k, int p, uint64_t* sl, uint64_t* sc, int lane)
+{
+    uint64_t v[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int t = lane * E + e;
+        v[e] = t < c ? cp[t] : kEmptyKey;
+    }
+    uint64_t* lp = lists + (size_t)p * k;
+    for (int t = lane; t < k; t += 32) sl[t] = lp[t];
+    warp_sort_regs<E>(v, lane);
+#pragma unroll
+    for (int e = 0; e < E; ++e) sc[lane * E + e] = v[e];
+    __syncwarp();
+    for (int r = lane; r < k; r += 32) {
+        const int i = merge_split(sl, k, sc, c, r);
+        const int j = r - i;
+        lp[r] = (i < k && (j >= c || sl[i] <= sc[j])) ? sl[i] : sc[j];
+    }
+}
+
+// one warp per point; k <= kSortedMergeMaxK and at most 512 candidates per point
+constexpr int kSortedMergeMaxK = 256;
+constexpr int kSortedMergeWarps = 8;
+
+__global__ void __launch_bounds__(kSortedMergeWarps * 32)
+    knn_merge_sorted_kernel(uint64_t* __restrict__ lists, uint64_t* __restrict__ thr, float* __restrict__ U,
+                            const float* __restrict__ norms, const uint64_t* __restrict__ cand,
+                            int* __restrict__ cnt, int n, int k, int cap, int d, int kp, int exact,
+                            unsigned long long* __restrict__ admitted, unsigned char* __restrict__ aimg,
+                            const float* __restrict__ ntf)
+{
+    __shared__ uint64_t sl_all[kSortedMergeWarps][kSortedMergeMaxK];
+    __shared__ uint64_t sc_all[kSortedMergeWarps][512];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int p = blockIdx.x * kSortedMergeWarps + w;
+    if (p >= n) return;
+    int c = cnt[p];
+    if (c == 0) return;
+    c = min(c, cap);
+    const uint64_t* cp = cand + (size_t)p * cap;
+    uint64_t* sl = sl_all[w];
+    uint64_t* sc = sc_all[w];
+    if (c <= 32) merge_point_sorted<1>(lists, cp, c, k, p, sl, sc, lane);
+    else if (c <= 64) merge_point_sorted<2>(lists, cp, c, k, p, sl, sc, lane);
+    else if (c <= 128) merge_point_sorted<4>(lists, cp, c, k, p, sl, sc, lane);
+    else if (c <= 256) merge_point_sorted<8>(lists, cp, c, k, p, sl, sc, lane);
+    else merge_point_sorted<16>(lists, cp, c, k, p, sl, sc, lane);
+    __syncwarp();
+    if (lane == 0) {
+        const uint64_t t = lists[(size_t)p * k + k - 1];
+        thr[p] = t;
+        cnt[p] = 0;
+        const float T = (t == kEmptyKey) ? __int_as_float(0x7f800000) : __uint_as_float((uint32_t)(t >> 32));
+        if (aimg) {
+            float V, wv;
+            fold_bound(filter_bound(T, norms[p], d, kp, exact), ntf[p], kp, exact, V, wv);
+            U[p] = V;
+            store_fold(aimg, p, d, kp, wv);
+        }
+        atomicAdd(admitted, (unsigned long long)c);
+    }
+}
+
 // per-point state before the first round: empty lists admit everything, padding nothing
 __global__ void init_point_state_kernel(int n, int rows, float* __restrict__ norms, uint64_t* __restrict__ thr,
                                         float* __restrict__ U)
@@ -463,19 +583,27 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
             pending = ndelta / 2;
             continue;
         }
-        knn_merge_kernel<<<(n + mwarps - 1) / mwarps, mwarps * 32, msmem, s>>>(
-            lists, thr, U, norms, cand, cnt, n, k, cap, pw, d, kp, exact, admitted, fold.aimg, fold.ntf);
+        if (trace) FDB_CUDA(cudaEventRecord(t0, s));
+        if (k <= kSortedMergeMaxK && cap <= 512)
+            knn_merge_sorted_kernel<<<(n + kSortedMergeWarps - 1) / kSortedMergeWarps, kSortedMergeWarps * 32, 0, s>>>(
+                lists, thr, U, norms, cand, cnt, n, k, cap, d, kp, exact, admitted, fold.aimg, fold.ntf);
+        else
+            knn_merge_kernel<<<(n + mwarps - 1) / mwarps, mwarps * 32, msmem, s>>>(
+                lists, thr, U, norms, cand, cnt, n, k, cap, pw, d, kp, exact, admitted, fold.aimg, fold.ntf);
         FDB_LAUNCHED();
         if (trace) {
+            FDB_CUDA(cudaEventRecord(t1, s));
             unsigned long long adm = 0, cn[16] = {0};
             FDB_CUDA(cudaMemcpyAsync(&adm, admitted, sizeof(adm), cudaMemcpyDeviceToHost, s));
             FDB_CUDA(cudaMemcpyAsync(cn, counters, sizeof(cn), cudaMemcpyDeviceToHost, s));
             FDB_CUDA(cudaMemsetAsync(counters, 0, sizeof(cn), s));
             FDB_CUDA(cudaStreamSynchronize(s));
+            float merge_ms = 0.0f;
+            FDB_CUDA(cudaEventElapsedTime(&merge_ms, t0, t1));
             const double chunks = (double)units * 32.0;   // 8 warps x 4 chunks per 128 x 256 tile
-            fprintf(stderr, "[fdb200] round %d %s delta0=%d ndelta=%d units=%d tile_ms=%.3f admitted=%llu (%.1f/point)"
-                            " refined=%llu (%.2f/chunk) hit_chunks=%.1f%% drain_steps/hit_chunk=%.2f\n",
-                    res.rounds, r.diag ? "diag" : "offs", r.delta0, r.diag ? 0 : ndelta, units, ms,
+            fprintf(stderr, "[fdb200] round %d %s delta0=%d ndelta=%d units=%d tile_ms=%.3f merge_ms=%.3f admitted=%llu"
+                            " (%.1f/point) refined=%llu (%.2f/chunk) hit_chunks=%.1f%% drain_steps/hit_chunk=%.2f\n",
+                    res.rounds, r.diag ? "diag" : "offs", r.delta0, r.diag ? 0 : ndelta, units, ms, merge_ms,
                     adm - adm_before, (double)(adm - adm_before) / n, cn[0], cn[0] / chunks,
                     100.0 * cn[1] / chunks, cn[1] ? (double)cn[2] / cn[1] : 0.0);
             adm_before = adm;
