@@ -36,8 +36,8 @@ sys.path.insert(0, str(ROOT / "symwarp-fastdec_b200"))
 PUBLISHED_A6000_FIT_S = 16.49          # README.md:149, symwarp FP32 Fit seconds on GloVe 50d (A6000)
 # DRAM traffic of the tile kernels over one fit of the default workload, from one ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum summed over the nine knn_tile_tc launches of a fit:
-# 589.9 GB read + 20.2 GB written). A one-pass metric set, so it was taken on the full workload.
-TILE_DRAM_BYTES_PER_FIT = 610.03e9
+# 367.1 GB read + 17.3 GB written). A one-pass metric set, so it was taken on the full workload.
+TILE_DRAM_BYTES_PER_FIT = 384.36e9
 WORKLOAD = dict(n=1_291_147, d=50, k=45, c=20)
 
 
