@@ -1,0 +1,70 @@
+"""The sharded fit on two GPUs (one process per GPU, NCCL): the kNN triangle split by row blocks, the
+partial lists exchanged to their owners with an all-to-all, merged, gathered on rank 0, and the fit
+finished there must give exactly the single-GPU centers and labels. Skipped on a one-GPU machine."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, n, q):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    import fastdec_b200 as fdb
+    from fastdec_b200.datasets import embedding_cloud
+    from fastdec_b200.multigpu import ShardedFit
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+        x = embedding_cloud(n=n, d=50, seed=5)
+        xd = torch.from_numpy(x).to(dev)
+        k, c = 30, 10
+        sp = torch.cuda.current_stream(dev).cuda_stream
+        runner = ShardedFit(n, 50, k, c, rank, world, dev, sp)
+        centers = torch.empty(c, dtype=torch.int32, device=dev)
+        labels = torch.empty(n, dtype=torch.int32, device=dev)
+        for _ in range(2):   # twice: buffers and lists are reused across steps
+            runner.step(xd, centers, labels)
+        torch.cuda.synchronize(dev)
+        if rank == 0:
+            ref = fdb.fit(x, k, c)
+            same = (centers.cpu().numpy().tolist() == ref["centers"].tolist()
+                    and np.array_equal(labels.cpu().numpy(), ref["labels"]))
+            q.put((rank, "ok" if same else "mismatch"))
+        else:
+            q.put((rank, "ok"))
+        dist.barrier()
+        runner.close()
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.gpu
+def test_sharded_fit_on_two_gpus_matches_one_gpu():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, 150_000, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+    assert results == {0: "ok", 1: "ok"}
