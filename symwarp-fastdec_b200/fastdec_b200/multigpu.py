@@ -8,6 +8,10 @@ associative and commutative). Points are owned by contiguous ranges; one all-to-
 partial list to its owner, the owner merges the `world` copies on the GPU, and rank 0 gathers the
 merged ranges and runs the O(n k) tail (density, DC detection / reduction, labels) alone.
 
+With the tcgen05 engine a rank tests only the rows of its own blocks against every column block, so
+the lists of its own points are already complete and every other list it holds is empty: the
+all-to-all and the merge are skipped and each rank contributes its block rows to the gather.
+
 The exchange (`exchange_to_owners`, `gather_to_root`) only uses torch.distributed collectives, so
 the same code runs over NCCL on B200s and over gloo on CPU tensors in the tests.
 """
@@ -45,14 +49,21 @@ def exchange_to_owners(lists: torch.Tensor, rank: int, world: int) -> torch.Tens
     return out
 
 
-def gather_to_root(merged: torch.Tensor, n: int, rank: int, world: int):
-    """merged: (n_own, k) final lists of this rank's points. Rank 0 receives the full (n, k).
+def block_ranges(n: int, world: int, block: int = 128):
+    """[start, stop) of the points in each rank's row blocks (the split fdb200_knn_partial uses)."""
+    T = (n + block - 1) // block
+    return [(min(n, block * (T * r // world)), min(n, block * (T * (r + 1) // world))) for r in range(world)]
+
+
+def gather_to_root(merged: torch.Tensor, n: int, rank: int, world: int, ranges=None):
+    """merged: (n_own, k) final lists of this rank's points (its range in `ranges`, the owner ranges
+    by default). Rank 0 receives the full (n, k).
 
     A collective (all-gather of equal, padded blocks) rather than point-to-point sends: collectives on
     one communicator run in the same order on every rank, so a rank that has already moved on to
     the next step's kernels cannot hold back the transfer that rank 0 is waiting for."""
     k = merged.shape[1]
-    rng = owner_ranges(n, world)
+    rng = ranges if ranges is not None else owner_ranges(n, world)
     width = max(b - a for a, b in rng)
     pad = torch.empty((width, k), dtype=merged.dtype, device=merged.device)
     pad[:merged.shape[0]].copy_(merged)
@@ -81,15 +92,23 @@ class ShardedFit:
         fdb, n, k = self.fdb, self.n, self.k
         _log(self.rank, "step: partial kNN")
         st = fdb.knn_partial_device(x_dev, k, self.lists, (self.rank, self.world), stream=self.sp, **self.opts)
-        _log(self.rank, "step: exchange", st.get("knn_ms"))
-        blocks = exchange_to_owners(self.lists, self.rank, self.world)
-        n_own = blocks.shape[1]
-        _log(self.rank, "step: merge")
-        if n_own > 0:
-            fdb.merge_lists_device(blocks[0], blocks[1:], self.world - 1, n_own, k, stream=self.sp,
-                                   device=self.dev.index or 0)
-        _log(self.rank, "step: gather")
-        full = gather_to_root(blocks[0], n, self.rank, self.world)
+        n_own = 0
+        if st.get("engine_used") == 2:
+            # rows-only engine: this rank's block rows are final, nothing to exchange or merge
+            rng = block_ranges(n, self.world)
+            a, b = rng[self.rank]
+            _log(self.rank, "step: gather")
+            full = gather_to_root(self.lists[a:b], n, self.rank, self.world, rng)
+        else:
+            _log(self.rank, "step: exchange", st.get("knn_ms"))
+            blocks = exchange_to_owners(self.lists, self.rank, self.world)
+            n_own = blocks.shape[1]
+            _log(self.rank, "step: merge")
+            if n_own > 0:
+                fdb.merge_lists_device(blocks[0], blocks[1:], self.world - 1, n_own, k, stream=self.sp,
+                                       device=self.dev.index or 0)
+            _log(self.rank, "step: gather")
+            full = gather_to_root(blocks[0], n, self.rank, self.world)
         _log(self.rank, "step: tail")
         if self.rank == 0:
             fdb.lists_to_knn_device(full, n, k, self.dist, self.idx, stream=self.sp, device=self.dev.index or 0)

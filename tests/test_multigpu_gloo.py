@@ -89,3 +89,14 @@ def test_owner_ranges_cover_every_point_once():
             rng = owner_ranges(n, world)
             assert rng[0][0] == 0 and rng[-1][1] == n
             assert all(rng[i][1] == rng[i + 1][0] for i in range(world - 1))
+
+
+def test_block_ranges_follow_the_kernel_row_block_split():
+    from fastdec_b200.multigpu import block_ranges
+    for n in (1, 127, 128, 129, 1_291_147):
+        for world in (1, 2, 3, 8):
+            rng = block_ranges(n, world)
+            assert rng[0][0] == 0 and rng[-1][1] == n
+            assert all(rng[i][1] == rng[i + 1][0] for i in range(world - 1))
+            T = (n + 127) // 128
+            assert all(a == min(n, 128 * (T * r // world)) for r, (a, _) in enumerate(rng))
