@@ -45,7 +45,9 @@ typedef struct FdB200Opts {
     int precision;            /* FDB200_FP32: distances bit-identical to the reference FDS build
                                  (fmaf chain); FDB200_TF32: tensor-core TF32 distances */
     int density_kernel;       /* FDB200_LAPLACIAN (default) or FDB200_GAUSSIAN */
-    int engine;               /* which distance-tile engine runs the self-kNN */
+    int engine;               /* which distance-tile engine runs the self-kNN: AUTO = tcgen05 where
+                                 supported, with the first (dense) rounds on the exact SIMT tiles;
+                                 TCGEN05 = tcgen05 for every round; SIMT = SIMT for every round */
     int inputs_on_device;     /* nonzero: data / density / index inputs are device pointers */
     int outputs_on_device;    /* nonzero: outputs are device pointers */
     int shard_rank;           /* kNN triangle sharding: this shard's index ... */

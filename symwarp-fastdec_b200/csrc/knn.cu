@@ -55,6 +55,7 @@ void compute_norms(const float* x, int ldx, int n, int d, float* norms, cudaStre
 }
 
 constexpr int kSimtThreads = 256;
+constexpr int kSimtRoundMaxOffsets = 16;   // rounds of at most this many offsets run on the SIMT tiles
 constexpr int kDChunk = 32;
 
 // Exact FP32 tile: 128 x 128 pairs per CTA, 8 x 8 per thread, every dot product the sequential
@@ -556,7 +557,17 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
             units = nb * ndelta;
         }
         FDB_CUDA(cudaEventRecord(t0, s));
-        launch_tile_round(r, units, engine, cfg.precision, s);
+        // With the automatic engine, the first rounds run on the exact SIMT tiles: they offer every
+        // point few, mostly admissible candidates (its thresholds are still loose), so nearly every
+        // pair would be refined after the TF32 filter anyway (measured at the headline size: the
+        // diagonal and the first three offset rounds take 28 ms instead of 67 ms). An explicit
+        // tcgen05 request, and a sharded run (its rows-only bookkeeping needs one engine), keep
+        // tcgen05 for every round.
+        const int round_engine = (cfg.engine == FDB200_ENGINE_AUTO && engine == FDB200_ENGINE_TCGEN05 &&
+                                  cfg.shard_count == 1 && (r.diag || ndelta <= kSimtRoundMaxOffsets))
+                                     ? FDB200_ENGINE_SIMT
+                                     : engine;
+        launch_tile_round(r, units, round_engine, cfg.precision, s);
         FDB_CUDA(cudaEventRecord(t1, s));
         FDB_CUDA(cudaMemcpyAsync(ws.pinned, ovf, 2 * sizeof(int), cudaMemcpyDeviceToHost, s));
         FDB_CUDA(cudaStreamSynchronize(s));
@@ -607,7 +618,7 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
                     adm - adm_before, (double)(adm - adm_before) / n, cn[0], cn[0] / chunks,
                     100.0 * cn[1] / chunks, cn[1] ? (double)cn[2] / cn[1] : 0.0);
             adm_before = adm;
-            if (engine == FDB200_ENGINE_TCGEN05 && !r.diag) {
+            if (round_engine == FDB200_ENGINE_TCGEN05 && !r.diag) {
                 // per tcgen05 tile (counted by the MMA issuers), cycles per CTA role instance
                 const double tiles = cn[3] > 0 ? (double)cn[3] : 1.0;
                 const double per_f = tiles * 8.0;   // filter warp-tiles (each tile has one refine warp)
