@@ -1,6 +1,6 @@
 #!/usr/bin/env python
 """Benchmark of the hot path: the whole FastDEC fit (exact self-kNN -> density -> DC detection ->
-DC reduction -> labels) on the headline workload, 1,291,147 x 50 fp32, k=45, c=20 (
+DC reduction -> labels) on the headline workload, 1,291,147 x 50 fp32, k=45, c=20 (the reference's config 3,
 a seeded synthetic stand-in for GloVe 50d).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]

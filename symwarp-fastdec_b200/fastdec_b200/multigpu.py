@@ -1,6 +1,6 @@
 """Multi-GPU self-kNN: one process per GPU, the triangle sharded by row blocks.
 
-The reference is single-GPU (SURVEY: no NCCL/MPI anywhere). Here every rank evaluates the block
+The reference is single-GPU (its sources use no NCCL or MPI). Here every rank evaluates the block
 pairs of its share of the triangle (fdb200_knn_partial with shard = (rank, world)) into partial
 lists for ALL points; a partial list is a lexicographic (d2, index) k-smallest of the candidates the
 rank saw, so the k-smallest of all ranks' partial lists is the exact answer (the selection is
