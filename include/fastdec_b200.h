@@ -172,6 +172,17 @@ int fdb200_fit_from_knn(const float* data, const float* knn_dist_dev, const int*
 int fdb200_release(const FdB200Opts* opts);
 
 /*
+ * The reference CLI's dataset file: one point per line, comma-separated numbers. Replaces
+ * get_rows_coloumns + read_data (helper.cpp:9-63) and the host transpose (test.cpp:110-115), in
+ * parallel: fdb200_csv_shape gives the point count n (non-blank lines) and dimension d (values on the
+ * first line); fdb200_read_csv fills out_dim_major[t * n + i] (d * n floats, caller-allocated) with
+ * threads host threads (0 = all cores). Values parse as strtof does (correctly rounded); a line
+ * without exactly d numbers is FDB200_EINVAL. No GPU is involved.
+ */
+int fdb200_csv_shape(const char* path, int* n_out, int* d_out);
+int fdb200_read_csv(const char* path, int n, int d, float* out_dim_major, int threads);
+
+/*
  * fdb200_density without any allocation. No counterpart in the reference (every reference call,
  * and every other entry point here, obtains device memory as it goes). It is for callers that must
  * not allocate while they run: a serving loop that reserved all device memory up front, a process

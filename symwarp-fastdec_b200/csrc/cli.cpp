@@ -2,8 +2,8 @@
 //
 // Usage mirrors the reference CLI (test.cpp:185-357): [--gpu N] [--backend b200] [config_file],
 // config = 4 lines (CSV path, k, cluster count, run count; runs defaults to 1 when missing or
-// invalid, test.cpp:314-337). The CSV is read row-major and transposed to the dim-major layout
-// Fit takes (helper.cpp:9-63, test.cpp:110-115). Extra run-time switches replace the reference's
+// invalid, test.cpp:314-337). The CSV is read by the library in parallel straight into the
+// dim-major layout Fit takes (fdb200_read_csv; helper.cpp:9-63, test.cpp:110-115). Extra run-time switches replace the reference's
 // compile-time ones: --precision fp32|tf32 (USE_CUBLAS_TF32), --density laplacian|gaussian
 // (USE_GAUSSIAN_KERNEL), --engine auto|simt|tcgen05.
 #include <chrono>
@@ -22,36 +22,6 @@ static void usage(const char* prog)
     printf("Usage: %s [--gpu N] [--backend b200] [--precision fp32|tf32] [--density laplacian|gaussian]\n"
            "          [--engine auto|simt|tcgen05] [config_file]\n", prog);
     printf("  config_file    4 lines: dataset CSV, k, cluster count, run count (default ./config.txt)\n");
-}
-
-static bool read_csv(const std::string& path, std::vector<float>& rows, int& n, int& d)
-{
-    std::ifstream f(path);
-    if (!f) return false;
-    std::string line;
-    n = 0;
-    d = -1;
-    while (std::getline(f, line)) {
-        if (line.empty() || line == "\r") continue;
-        int cols = 0;
-        const char* p = line.c_str();
-        while (*p) {
-            char* end = nullptr;
-            const float v = strtof(p, &end);
-            if (end == p) break;
-            rows.push_back(v);
-            ++cols;
-            p = end;
-            while (*p == ',' || *p == ' ' || *p == '\r') ++p;
-        }
-        if (d < 0) d = cols;
-        if (cols != d) {
-            fprintf(stderr, "Error: row %d has %d columns, expected %d\n", n + 1, cols, d);
-            return false;
-        }
-        ++n;
-    }
-    return n > 0 && d > 0;
 }
 
 int main(int argc, char** argv)
@@ -118,19 +88,23 @@ int main(int argc, char** argv)
     printf("Read dataset from: %s\nNumber of nearest neighbors: %d\nNumber of clusters: %d\n"
            "Number of runs: %d\nBackend: b200\n", data_file.c_str(), k, c, runs);
 
-    std::vector<float> rows;
     int n = 0, d = 0;
-    if (!read_csv(data_file, rows, n, d)) {
-        printf("Error: could not read %s\n", data_file.c_str());
+    const auto tr0 = std::chrono::steady_clock::now();
+    if (fdb200_csv_shape(data_file.c_str(), &n, &d) != FDB200_OK) {
+        printf("Error: could not read %s: %s\n", data_file.c_str(), fdb200_last_error());
         return EXIT_FAILURE;
     }
+    std::vector<float> dm((size_t)n * d);   // dim-major, as Fit takes it (test.cpp:110-115)
+    if (fdb200_read_csv(data_file.c_str(), n, d, dm.data(), 0) != FDB200_OK) {
+        printf("Error: could not read %s: %s\n", data_file.c_str(), fdb200_last_error());
+        return EXIT_FAILURE;
+    }
+    printf("Read %d points of dimension %d in %.3f s\n", n, d,
+           std::chrono::duration<double>(std::chrono::steady_clock::now() - tr0).count());
     if (n < k) {
         printf("Error: k value is larger that the number of reference points\n");
         return EXIT_FAILURE;
     }
-    std::vector<float> dm((size_t)n * d);
-    for (int i = 0; i < n; ++i)
-        for (int t = 0; t < d; ++t) dm[(size_t)t * n + i] = rows[(size_t)i * d + t];
 
     for (int run = 1; run <= runs; ++run) {
         try {

@@ -63,7 +63,7 @@ class Stats(ctypes.Structure):
 EXPORTS = ["fdb200_opts_init", "fdb200_last_error", "fdb200_abi_version", "fdb200_knn", "fdb200_fit",
            "fdb200_dc_reduction", "fdb200_density", "fdb200_dc_detection", "fdb200_final_cluster",
            "fdb200_knn_partial", "fdb200_merge_lists", "fdb200_lists_to_knn", "fdb200_fit_from_knn",
-           "fdb200_release", "fdb200_density_noalloc"]
+           "fdb200_release", "fdb200_density_noalloc", "fdb200_csv_shape", "fdb200_read_csv"]
 
 _lib = None
 
@@ -155,6 +155,17 @@ def knn(data_dm, k, **kw):
     _check(lib().fdb200_knn(_ptr(x), n, d, k, ctypes.byref(make_opts(**kw)), _ptr(dist), _ptr(idx),
                             ctypes.byref(st)))
     return dist, idx, st.as_dict()
+
+
+def read_csv(path, threads=0):
+    """The reference CLI's dataset file (one point per line, comma-separated) as a dim-major
+    (d, n) float32 array, parsed in parallel by the library (fdb200_csv_shape / fdb200_read_csv)."""
+    n, d = ctypes.c_int(0), ctypes.c_int(0)
+    p = str(path).encode()
+    _check(lib().fdb200_csv_shape(p, ctypes.byref(n), ctypes.byref(d)))
+    out = np.empty((d.value, n.value), np.float32)
+    _check(lib().fdb200_read_csv(p, n.value, d.value, _ptr(out), int(threads)))
+    return out
 
 
 def fit(data_dm, k, c, **kw):
