@@ -68,3 +68,13 @@ def test_tf32_mode_distances_close(fdb, oracle):
     recall = np.mean([len(set(idx[:, i]) & set(oi[:, i])) / 20 for i in range(8000)])
     assert recall > 0.95
     assert (np.diff(dist, axis=0) >= 0).all()
+
+
+def test_auto_engine_mixes_rounds_and_stays_exact(fdb):
+    """The automatic engine runs the first (dense) rounds on the SIMT tiles and the rest on tcgen05;
+    the lists must be identical to an all-tcgen05 and an all-SIMT run."""
+    x = ds.embedding_cloud(n=120_000, d=50, seed=13)
+    a = fdb.knn(x, 45)
+    b = fdb.knn(x, 45, engine="tcgen05")
+    assert a[2]["engine_used"] == 2 and a[2]["rounds"] == b[2]["rounds"]
+    assert np.array_equal(a[1], b[1]) and np.array_equal(a[0], b[0])
