@@ -73,7 +73,6 @@ struct Args {
     int b_lo, nb;                // row blocks of this shard
     int r0[2], len[2], np[2];    // forward / backward offset ranges: first offset, length, pairs
     int ppi, nchunk0, items;     // pairs per work item, items of the forward range, all items
-    const float* V;              // folded filter bounds
     const float* nrm;            // exact fp32 norms
     const uint64_t* thr;         // exact admission thresholds
     const float* xp;             // original coordinates, point-major, dp floats per row
@@ -118,8 +117,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity)
 
 // trace-mode phase timers: cycles accumulated per role, added to counters[4 + slot] at the end
 enum {
-    kTProdWaitCols, kTProdWaitRows, kTMmaWaitCols, kTMmaWaitRows, kTMmaWaitAcc, kTFiltWait, kTFiltWork, kTRefWait,
-    kTRefWork, kTNum
+    kTProdWaitCols = 0, kTProdWaitRows = 1, kTFiltWait = 5, kTFiltWork = 6, kTRefWait = 7, kTRefWork = 8
 };
 
 // bounded wait: false on timeout or when another role aborted the CTA
@@ -764,7 +762,7 @@ struct TcState {
     int n = 0, d = 0, kp = 0, dp = 0, npad = 0, sms = 0, stages = 0;
     unsigned char *A = nullptr, *B = nullptr;
     float *xp = nullptr, *ntf = nullptr;
-    float *V = nullptr, *nrm = nullptr;   // V / nrm / thr belong to the scheduler
+    float* nrm = nullptr;   // nrm / thr belong to the scheduler
     uint64_t* thr = nullptr;
 };
 
@@ -817,7 +815,7 @@ TcFold tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const fl
     st.dp = dp;
     st.npad = npad;
     st.stages = tc::pick_stages(kp);
-    st.V = const_cast<float*>(U);
+    (void)U;   // the folded bounds live in the row image; the scheduler keeps V for its own use
     st.nrm = const_cast<float*>(norms);
     st.thr = const_cast<uint64_t*>(thr);
     TcFold f;
@@ -842,7 +840,6 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.diag = r.diag;
     a.b_lo = r.b_lo;
     a.nb = r.nb;
-    a.V = st.V;
     a.nrm = st.nrm;
     a.thr = st.thr;
     a.xp = st.xp;
