@@ -30,6 +30,7 @@
 #include <cfloat>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <vector>
 
 namespace fdb {
@@ -64,6 +65,11 @@ __global__ void __launch_bounds__(kSimtThreads, 2) knn_tile_simt(TileRound r)
 {
     __shared__ __align__(16) float As[kDChunk][kBlock];
     __shared__ __align__(16) float Bs[kDChunk][kBlock];
+    // rounds are queued without a host check in between: once an earlier round overflowed (or this
+    // one did, in another CTA), the round is discarded and the CTA does nothing (one read, made
+    // uniform across the CTA)
+    if (__syncthreads_or(threadIdx.x == 0 && (*(volatile const int*)r.ovf | *((volatile const int*)r.ovf + 1))))
+        return;
     int B, R;
     if (!decode_unit(r, blockIdx.x, B, R)) return;
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -188,9 +194,10 @@ __global__ void knn_merge_kernel(uint64_t* __restrict__ lists, uint64_t* __restr
                                  const uint64_t* __restrict__ cand, int* __restrict__ cnt, int n,
                                  int k, int cap, int pw, int d, int kp, int exact,
                                  unsigned long long* __restrict__ admitted, unsigned char* __restrict__ aimg,
-                                 const float* __restrict__ ntf)
+                                 const float* __restrict__ ntf, const int* __restrict__ stop)
 {
     extern __shared__ uint64_t msm[];
+    if (stop[0] | stop[1]) return;   // the round overflowed or an earlier one stopped: lists stay as they are
     const int warps = blockDim.x >> 5, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int p = blockIdx.x * warps + w;
     if (p >= n) return;
@@ -308,10 +315,11 @@ __global__ void __launch_bounds__(kSortedMergeWarps * 32)
                             const float* __restrict__ norms, const uint64_t* __restrict__ cand,
                             int* __restrict__ cnt, int n, int k, int cap, int d, int kp, int exact,
                             unsigned long long* __restrict__ admitted, unsigned char* __restrict__ aimg,
-                            const float* __restrict__ ntf)
+                            const float* __restrict__ ntf, const int* __restrict__ stop)
 {
     __shared__ uint64_t sl_all[kSortedMergeWarps][kSortedMergeMaxK];
     __shared__ uint64_t sc_all[kSortedMergeWarps][512];
+    if (stop[0] | stop[1]) return;   // the round overflowed or an earlier one stopped: lists stay as they are
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int p = blockIdx.x * kSortedMergeWarps + w;
     if (p >= n) return;
@@ -458,6 +466,24 @@ static long long shard_pairs(int n, int T, int b_lo, int b_hi)
     return tot;
 }
 
+// timing events, created on first use and destroyed with the pool (also when a round throws)
+struct EventPool {
+    std::vector<cudaEvent_t> ev;
+    cudaEvent_t get(int i)
+    {
+        while ((int)ev.size() <= i) {
+            cudaEvent_t e;
+            FDB_CUDA(cudaEventCreate(&e));
+            ev.push_back(e);
+        }
+        return ev[i];
+    }
+    ~EventPool()
+    {
+        for (cudaEvent_t e : ev) cudaEventDestroy(e);
+    }
+};
+
 static void launch_tile_round(const TileRound& r, int units, int engine, int precision, cudaStream_t s)
 {
     if (engine == FDB200_ENGINE_TCGEN05) launch_tile_round_tc(r, units, precision, s);
@@ -522,103 +548,118 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     r.x = x; r.ldx = cfg.ldx; r.n = n; r.d = d; r.norms = norms; r.thr = thr; r.U = U; r.cand = cand;
     r.cnt = cnt; r.cap = cap; r.ovf = ovf; r.T = T; r.b_lo = b_lo; r.nb = nb;
 
-    cudaEvent_t t0, t1;
-    FDB_CUDA(cudaEventCreate(&t0));
-    FDB_CUDA(cudaEventCreate(&t1));
+    // Rounds are queued back to back with no host check in between: the schedule below depends only on
+    // host state, each tile kernel tags an overflow with its round, and every later kernel of the batch
+    // sees the flag and does nothing. One settle per batch (normally one per fit) reads the flags; an
+    // overflowed round is re-planned in halves from where it started, which is exact because lists only
+    // change in the merges of rounds that completed. Host stalls between launches therefore do not
+    // leave the device idle.
+    struct Planned {
+        int diag, delta0, ndelta, units, engine;
+        double seen;   // the `seen` estimate before the round
+    };
+    std::vector<Planned> plan;
+    EventPool ev;
     const int dmax = T / 2;
     const char* trace_env = getenv("FDB200_TRACE");
     const bool trace = trace_env && trace_env[0] == '1';
-    unsigned long long adm_before = 0;
+    unsigned long long adm_before = 0, adm = 0;
     unsigned long long* counters = ws.misc2.as<unsigned long long>(16);   // trace counters
     r.counters = trace ? counters : nullptr;
     if (trace) FDB_CUDA(cudaMemsetAsync(counters, 0, 16 * sizeof(unsigned long long), s));
     bool diag_done = false;
     int next_delta = 1;
     double seen = kBlock - 1;   // candidates each point has been offered so far (approximate)
-    int pending = 0;            // block offsets in the round being retried, 0 = none
-    while (nb > 0 && (!diag_done || next_delta <= dmax)) {
-        int units, ndelta = 0;
-        if (!diag_done) {
-            r.diag = 1;
-            r.delta0 = 0;
-            r.ndelta = 0;
-            units = nb;
-        } else {
-            if (pending > 0) {
-                ndelta = pending;
+    int pending = 0;            // block offsets of a round being re-planned, 0 = none
+    cudaEvent_t m0 = ev.get(0), m1 = ev.get(1);   // trace: merge timing
+    for (;;) {
+        const bool more = nb > 0 && (!diag_done || next_delta <= dmax);
+        if (more) {
+            Planned pl{};
+            pl.seen = seen;
+            if (!diag_done) {
+                pl.diag = 1;
+                pl.units = nb;
             } else {
-                // expected admissions per point ~ new * k / seen; keep them near cap / 4
-                const double want = (double)cap * seen / (8.0 * kBlock * k);
-                ndelta = (int)std::max(1.0, std::min(want, (double)(dmax - next_delta + 1)));
+                if (pending > 0) {
+                    pl.ndelta = pending;
+                } else {
+                    // expected admissions per point ~ new * k / seen; keep them near cap / 4
+                    const double want = (double)cap * seen / (8.0 * kBlock * k);
+                    pl.ndelta = (int)std::max(1.0, std::min(want, (double)(dmax - next_delta + 1)));
+                }
+                pl.delta0 = next_delta;
+                pl.units = nb * pl.ndelta;
             }
-            r.diag = 0;
-            r.delta0 = next_delta;
-            r.ndelta = ndelta;
-            units = nb * ndelta;
+            // With the automatic engine, the first rounds run on the exact SIMT tiles: they offer every
+            // point few, mostly admissible candidates (its thresholds are still loose), so nearly every
+            // pair would be refined after the TF32 filter anyway (measured at the headline size: the
+            // diagonal and the first three offset rounds take 28 ms instead of 67 ms). An explicit
+            // tcgen05 request, and a sharded run (its rows-only bookkeeping needs one engine), keep
+            // tcgen05 for every round.
+            pl.engine = (cfg.engine == FDB200_ENGINE_AUTO && engine == FDB200_ENGINE_TCGEN05 &&
+                         cfg.shard_count == 1 && (pl.diag || pl.ndelta <= kSimtRoundMaxOffsets))
+                            ? FDB200_ENGINE_SIMT
+                            : engine;
+            plan.push_back(pl);
+            const int slot = (int)plan.size();
+            r.diag = pl.diag;
+            r.delta0 = pl.delta0;
+            r.ndelta = pl.ndelta;
+            r.tag = slot;
+            FDB_CUDA(cudaEventRecord(ev.get(2 * slot), s));
+            launch_tile_round(r, pl.units, pl.engine, cfg.precision, s);
+            FDB_CUDA(cudaEventRecord(ev.get(2 * slot + 1), s));
+            if (trace) FDB_CUDA(cudaEventRecord(m0, s));
+            if (k <= kSortedMergeMaxK && cap <= 512)
+                knn_merge_sorted_kernel<<<(n + kSortedMergeWarps - 1) / kSortedMergeWarps, kSortedMergeWarps * 32, 0, s>>>(
+                    lists, thr, U, norms, cand, cnt, n, k, cap, d, kp, exact, admitted, fold.aimg, fold.ntf, ovf);
+            else
+                knn_merge_kernel<<<(n + mwarps - 1) / mwarps, mwarps * 32, msmem, s>>>(
+                    lists, thr, U, norms, cand, cnt, n, k, cap, pw, d, kp, exact, admitted, fold.aimg, fold.ntf, ovf);
+            FDB_LAUNCHED();
+            if (trace) FDB_CUDA(cudaEventRecord(m1, s));
+            if (!diag_done) {
+                diag_done = true;
+            } else {
+                next_delta += pl.ndelta;
+                seen += 2.0 * kBlock * pl.ndelta;
+                pending = 0;
+            }
+            if (!trace) continue;   // keep queueing; a trace settles (and prints) every round
         }
-        FDB_CUDA(cudaEventRecord(t0, s));
-        // With the automatic engine, the first rounds run on the exact SIMT tiles: they offer every
-        // point few, mostly admissible candidates (its thresholds are still loose), so nearly every
-        // pair would be refined after the TF32 filter anyway (measured at the headline size: the
-        // diagonal and the first three offset rounds take 28 ms instead of 67 ms). An explicit
-        // tcgen05 request, and a sharded run (its rows-only bookkeeping needs one engine), keep
-        // tcgen05 for every round.
-        const int round_engine = (cfg.engine == FDB200_ENGINE_AUTO && engine == FDB200_ENGINE_TCGEN05 &&
-                                  cfg.shard_count == 1 && (r.diag || ndelta <= kSimtRoundMaxOffsets))
-                                     ? FDB200_ENGINE_SIMT
-                                     : engine;
-        launch_tile_round(r, units, round_engine, cfg.precision, s);
-        FDB_CUDA(cudaEventRecord(t1, s));
-        FDB_CUDA(cudaMemcpyAsync(ws.pinned, ovf, 2 * sizeof(int), cudaMemcpyDeviceToHost, s));
+        if (plan.empty()) break;
+
+        // settle the batch: flags and the admitted counter in one copy
+        FDB_CUDA(cudaMemcpyAsync(ws.pinned, ovf, 4 * sizeof(int), cudaMemcpyDeviceToHost, s));
+        unsigned long long cn[16] = {0};
+        if (trace) FDB_CUDA(cudaMemcpyAsync(cn, counters, sizeof(cn), cudaMemcpyDeviceToHost, s));
+        if (trace) FDB_CUDA(cudaMemsetAsync(counters, 0, sizeof(cn), s));
         FDB_CUDA(cudaStreamSynchronize(s));
-        float ms = 0.0f;
-        FDB_CUDA(cudaEventElapsedTime(&ms, t0, t1));
-        res.tile_ms += ms;
-        res.rounds++;
-        if (ws.pinned[1]) {
-            cudaEventDestroy(t0);
-            cudaEventDestroy(t1);
-            throw Error(FDB200_EINTERNAL, "tcgen05 tile kernel stopped on a bounded wait (code " +
-                                              std::to_string(ws.pinned[1]) + ")");
+        const int tag = ws.pinned[0], err = ws.pinned[1];
+        std::memcpy(&adm, ws.pinned + 2, sizeof(adm));
+        const int ran = tag > 0 ? tag : (int)plan.size();   // rounds after an overflowed one did nothing
+        for (int i = 1; i <= (int)plan.size(); ++i) {
+            float ms = 0.0f;
+            FDB_CUDA(cudaEventElapsedTime(&ms, ev.get(2 * i), ev.get(2 * i + 1)));
+            res.tile_ms += ms;
         }
-        if (ws.pinned[0]) {
-            // discard the round: lists are untouched until the merge, so re-running is exact
-            res.overflow_reruns++;
-            FDB_CUDA(cudaMemsetAsync(cnt, 0, sizeof(int) * (size_t)n, s));
-            FDB_CUDA(cudaMemsetAsync(ovf, 0, sizeof(int), s));
-            if (r.diag || ndelta <= 1) {
-                cudaEventDestroy(t0);
-                cudaEventDestroy(t1);
-                throw Error(FDB200_EINTERNAL, "candidate buffer overflow on a single-offset round");
-            }
-            pending = ndelta / 2;
-            continue;
-        }
-        if (trace) FDB_CUDA(cudaEventRecord(t0, s));
-        if (k <= kSortedMergeMaxK && cap <= 512)
-            knn_merge_sorted_kernel<<<(n + kSortedMergeWarps - 1) / kSortedMergeWarps, kSortedMergeWarps * 32, 0, s>>>(
-                lists, thr, U, norms, cand, cnt, n, k, cap, d, kp, exact, admitted, fold.aimg, fold.ntf);
-        else
-            knn_merge_kernel<<<(n + mwarps - 1) / mwarps, mwarps * 32, msmem, s>>>(
-                lists, thr, U, norms, cand, cnt, n, k, cap, pw, d, kp, exact, admitted, fold.aimg, fold.ntf);
-        FDB_LAUNCHED();
+        res.rounds += ran;
+        if (err) throw Error(FDB200_EINTERNAL, "tcgen05 tile kernel stopped on a bounded wait (code " +
+                                                   std::to_string(err) + ")");
         if (trace) {
-            FDB_CUDA(cudaEventRecord(t1, s));
-            unsigned long long adm = 0, cn[16] = {0};
-            FDB_CUDA(cudaMemcpyAsync(&adm, admitted, sizeof(adm), cudaMemcpyDeviceToHost, s));
-            FDB_CUDA(cudaMemcpyAsync(cn, counters, sizeof(cn), cudaMemcpyDeviceToHost, s));
-            FDB_CUDA(cudaMemsetAsync(counters, 0, sizeof(cn), s));
-            FDB_CUDA(cudaStreamSynchronize(s));
-            float merge_ms = 0.0f;
-            FDB_CUDA(cudaEventElapsedTime(&merge_ms, t0, t1));
-            const double chunks = (double)units * 32.0;   // 8 warps x 4 chunks per 128 x 256 tile
+            const Planned& pl = plan.back();
+            float ms = 0.0f, merge_ms = 0.0f;
+            FDB_CUDA(cudaEventElapsedTime(&ms, ev.get(2), ev.get(3)));
+            FDB_CUDA(cudaEventElapsedTime(&merge_ms, m0, m1));
+            const double chunks = (double)pl.units * 32.0;   // 8 warps x 4 chunks per 128 x 256 tile
             fprintf(stderr, "[fdb200] round %d %s delta0=%d ndelta=%d units=%d tile_ms=%.3f merge_ms=%.3f admitted=%llu"
-                            " (%.1f/point) refined=%llu (%.2f/chunk) hit_chunks=%.1f%% drain_steps/hit_chunk=%.2f\n",
-                    res.rounds, r.diag ? "diag" : "offs", r.delta0, r.diag ? 0 : ndelta, units, ms, merge_ms,
+                            " (%.1f/point) refined=%llu (%.2f/chunk) hit_chunks=%.1f%% drain_steps/hit_chunk=%.2f%s\n",
+                    res.rounds, pl.diag ? "diag" : "offs", pl.delta0, pl.ndelta, pl.units, ms, merge_ms,
                     adm - adm_before, (double)(adm - adm_before) / n, cn[0], cn[0] / chunks,
-                    100.0 * cn[1] / chunks, cn[1] ? (double)cn[2] / cn[1] : 0.0);
+                    100.0 * cn[1] / chunks, cn[1] ? (double)cn[2] / cn[1] : 0.0, tag ? " (overflow)" : "");
             adm_before = adm;
-            if (round_engine == FDB200_ENGINE_TCGEN05 && !r.diag) {
+            if (pl.engine == FDB200_ENGINE_TCGEN05 && !pl.diag) {
                 // per tcgen05 tile (counted by the MMA issuers), cycles per CTA role instance
                 const double tiles = cn[3] > 0 ? (double)cn[3] : 1.0;
                 const double per_f = tiles * 8.0;   // filter warp-tiles (each tile has one refine warp)
@@ -628,19 +669,21 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
                         cn[0] / tiles, cn[1], cn[15] / tiles);
             }
         }
-        if (!diag_done) {
+        if (tag > 0) {
+            // re-plan the overflowed round in halves; its partial appends are dropped
+            const Planned pl = plan[tag - 1];
+            res.overflow_reruns++;
+            FDB_CUDA(cudaMemsetAsync(cnt, 0, sizeof(int) * (size_t)n, s));
+            FDB_CUDA(cudaMemsetAsync(ovf, 0, sizeof(int), s));
+            if (pl.diag || pl.ndelta <= 1)
+                throw Error(FDB200_EINTERNAL, "candidate buffer overflow on a single-offset round");
             diag_done = true;
-        } else {
-            next_delta += ndelta;
-            seen += 2.0 * kBlock * ndelta;
-            pending = 0;
+            next_delta = pl.delta0;
+            seen = pl.seen;
+            pending = pl.ndelta / 2;
         }
+        plan.clear();
     }
-    cudaEventDestroy(t0);
-    cudaEventDestroy(t1);
-    unsigned long long adm = 0;
-    FDB_CUDA(cudaMemcpyAsync(&adm, admitted, sizeof(adm), cudaMemcpyDeviceToHost, s));
-    FDB_CUDA(cudaStreamSynchronize(s));
     res.candidates = (long long)adm;
     return res;
 }

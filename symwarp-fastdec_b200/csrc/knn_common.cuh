@@ -26,7 +26,8 @@ struct TileRound {
     uint64_t* cand;          // n * cap candidate slots
     int* cnt;                // per-point slot counters
     int cap;
-    int* ovf;                // set when any counter passes cap
+    int* ovf;                // [0]: tag of the round in which a counter passed cap; [1]: tcgen05 error
+    int tag;                 // this round's tag (its index in the host's batch of rounds + 1)
     int T;                   // blocks in the triangle
     int b_lo, nb;            // this shard's row blocks
     int diag;                // 1: diagonal units (B, B), row side only
@@ -54,17 +55,7 @@ __device__ __forceinline__ bool decode_unit(const TileRound& r, int u, int& B, i
 __device__ __forceinline__ void append_at(const TileRound& r, int p, int slot, uint64_t key)
 {
     if (slot < r.cap) r.cand[(size_t)p * r.cap + slot] = key;
-    else atomicOr(r.ovf, 1);
-}
-
-__device__ __forceinline__ void append_keys(const TileRound& r, int p, const uint64_t* keys, int count)
-{
-    const int base = atomicAdd(&r.cnt[p], count);
-    for (int t = 0; t < count; ++t) {
-        const int slot = base + t;
-        if (slot < r.cap) r.cand[(size_t)p * r.cap + slot] = keys[t];
-        else atomicOr(r.ovf, 1);
-    }
+    else atomicExch(r.ovf, r.tag);
 }
 
 // K of the tcgen05 operand rows: D coordinates + 3 norm columns + 3 ones, padded to 8

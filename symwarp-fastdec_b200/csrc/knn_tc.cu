@@ -46,6 +46,7 @@
 #include "knn_common.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 
@@ -80,8 +81,9 @@ struct Args {
     const unsigned char* bimg;   // column operand, same layout
     uint64_t* cand;
     int* cnt;
-    int* ovf;
-    int* err;
+    int* ovf;                       // set to tag when a point's candidate count passes cap
+    int* err;                       // bounded-wait failure code
+    int tag;                        // the round's tag (its index in the host's batch + 1)
     unsigned long long* counters;   // optional trace counters
 };
 
@@ -307,7 +309,7 @@ __device__ __forceinline__ void tc_append(const Args& a, int p, uint64_t key)
 {
     const int slot = atomicAdd(&a.cnt[p], 1);
     if (slot < a.cap) a.cand[(size_t)p * a.cap + slot] = key;
-    else atomicOr(a.ovf, 1);
+    else atomicExch(a.ovf, a.tag);
 }
 
 // exact d2 of two points from the point-major original coordinates: fmaf chain over d = 0..D-1
@@ -364,6 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
     uint64_t* drain = q_free + kQueues;              // MMA completion before an early exit
     volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + P.misc);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + P.misc + 16);
+    volatile int* skip_flag = reinterpret_cast<volatile int*>(sm + P.misc + 32);
     int* qcount = reinterpret_cast<int*>(sm + P.qcount);
     int* qbase = reinterpret_cast<int*>(sm + P.queue);
 
@@ -385,8 +388,13 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
+        // rounds are queued without a host check in between: once an earlier round overflowed or
+        // stopped, this one is discarded too and does nothing
+        *skip_flag = (*(volatile const int*)a.ovf | *(volatile const int*)a.err) ? 1 : 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    __syncthreads();
+    if (*skip_flag) return;
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
                      "r"(512)
@@ -772,12 +780,22 @@ TcState g_state;   // the prepared operands of the current kNN call (one per pro
 
 bool tc_engine_supported(int d)
 {
+    // compute capability per device, read once (two attribute queries; the full property query
+    // costs milliseconds and would run on every call)
+    static std::atomic<int> cc[64] = {};
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return false;
-    cudaDeviceProp p;
-    if (cudaGetDeviceProperties(&p, dev) != cudaSuccess) return false;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return false;
+    int v = dev < 64 ? cc[dev].load() : 0;
+    if (v == 0) {
+        int major = 0, minor = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+            return false;
+        v = major * 10 + minor;
+        if (dev < 64) cc[dev].store(v);
+    }
     const int kp = tc_kp(d);
-    return p.major == 10 && p.minor == 0 && kp <= tc::kMaxKp && tc::pick_stages(kp) > 0;
+    return v == 100 && kp <= tc::kMaxKp && tc::pick_stages(kp) > 0;
 }
 
 // Prepares the TF32 operand images, the TF32 norms and the point-major original coordinates for
@@ -849,6 +867,7 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.cnt = r.cnt;
     a.ovf = r.ovf;
     a.err = r.ovf + 1;
+    a.tag = r.tag;
     a.counters = r.counters;
     if (r.diag) {
         a.items = r.nb;
