@@ -46,8 +46,9 @@ typedef struct FdB200Opts {
                                  (fmaf chain); FDB200_TF32: tensor-core TF32 distances */
     int density_kernel;       /* FDB200_LAPLACIAN (default) or FDB200_GAUSSIAN */
     int engine;               /* which distance-tile engine runs the self-kNN: AUTO = tcgen05 where
-                                 supported, with the first (dense) rounds on the exact SIMT tiles;
-                                 TCGEN05 = tcgen05 for every round; SIMT = SIMT for every round */
+                                 supported (sm_100 and d <= 154), with the first (dense) rounds on
+                                 the exact SIMT tiles; TCGEN05 = tcgen05 for every round; SIMT =
+                                 SIMT for every round (any d; FP32 only) */
     int inputs_on_device;     /* nonzero: data / density / index inputs are device pointers */
     int outputs_on_device;    /* nonzero: outputs are device pointers */
     int shard_rank;           /* kNN triangle sharding: this shard's index ... */

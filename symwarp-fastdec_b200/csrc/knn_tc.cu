@@ -59,17 +59,18 @@ constexpr int kRefineWarps = 6;
 constexpr int kThreads = 32 * (2 + kFilterWarps + kRefineWarps);
 constexpr int kRows = 128;               // rows per tile (one block)
 constexpr int kCols = 256;               // columns per tile (two blocks)
-constexpr int kMaxStages = 4;            // row block stages in shared memory
+constexpr int kMaxStages = 8;            // row stages in shared memory
 constexpr int kQueues = 8;               // survivor queues between filter and refine warps
 constexpr int kQueueCap = 256;           // entries per queue
 constexpr int kSlots = kQueueCap / kFilterWarps;   // a filter warp's share of one queue
 constexpr int kRawPerWarp = 4;           // survivor rows a filter warp may park raw per tile
-constexpr int kMaxKp = 64;               // K up to 64 floats (eight 32-byte panels)
+constexpr int kMaxKp = 256;              // K bound; what fits in shared memory decides (pick_plan)
 constexpr long long kWaitCycles = 2000000000ll;   // ~1 s at 2 GHz
 constexpr float kPoisonNorm = 1.2676506002282294e30f;   // 2^100, exact in TF32
 
 struct Args {
     int n, d, kp, dp, T, stages, cap, exact;
+    int gp, ng;                  // K panels per row stage, row stages per tile (ng * gp >= kp / 8)
     int diag;                    // 1: the diagonal round (X against X)
     int b_lo, nb;                // row blocks of this shard
     int r0[2], len[2], np[2];    // forward / backward offset ranges: first offset, length, pairs
@@ -230,7 +231,7 @@ struct Smem {
     uint32_t cols, rows[kMaxStages], queue, qcount, raw, bars, misc, total;
 };
 
-__host__ __device__ inline Smem smem_plan(int kp, int stages)
+__host__ __device__ inline Smem smem_plan(int kp, int stages, int gp)
 {
     Smem s;
     const uint32_t panels = (uint32_t)kp / 8;
@@ -238,8 +239,8 @@ __host__ __device__ inline Smem smem_plan(int kp, int stages)
     s.cols = o;                        // panel p: column block Y (4 KB) then Y + 1 (4 KB)
     o += panels * kCols * 32;
     for (int q = 0; q < kMaxStages; ++q) {
-        s.rows[q] = o;
-        if (q < stages) o += panels * kRows * 32;
+        s.rows[q] = o;                 // gp panels of one row block
+        if (q < stages) o += (uint32_t)gp * kRows * 32;
     }
     s.queue = o;                       // per queue: rows[cap], first columns[cap], masks[cap]; filter
     o += (uint32_t)kQueues * kQueueCap * 12u;   // warp e owns entries [e * kSlots, (e + 1) * kSlots)
@@ -249,19 +250,48 @@ __host__ __device__ inline Smem smem_plan(int kp, int stages)
     s.raw = o;                         // per queue and filter warp: kRawPerWarp rows of 32 words
     o += (uint32_t)kQueues * kFilterWarps * kRawPerWarp * 128u;
     s.bars = o;
-    o += 32 * 8;
+    o += 48 * 8;
     s.misc = o;
     o += 64;
     s.total = o;
     return s;
 }
 
-// the most row stages (2..4) whose plan fits the 227 KB a CTA may use; 0 if none
-inline int pick_stages(int kp)
+struct StagePlan {
+    int stages = 0, gp = 0;   // 0 stages: the shape does not fit
+};
+
+// How row blocks are staged. While two or more whole row blocks fit next to the resident column
+// pair (K <= 72), a stage holds one block (up to 4 stages) and every tile is one stage. For larger
+// K the column pair takes most of the 227 KB a CTA may use, so a stage holds gp consecutive K panels
+// of a block and a tile takes ceil(panels / gp) stages; the plan with the most panels in flight
+// ahead of the MMA wins, single-panel stages (twice the barrier traffic) only when no other fits.
+inline StagePlan pick_plan(int kp)
 {
-    for (int st = kMaxStages; st >= 2; --st)
-        if (smem_plan(kp, st).total + 1024 <= 227u * 1024u) return st;
-    return 0;
+    const uint32_t limit = 227u * 1024u - 1024u;
+    const int panels = kp / 8;
+    StagePlan best;
+    if (kp > kMaxKp || kp % 8) return best;
+    for (int st = 4; st >= 2; --st)
+        if (smem_plan(kp, st, panels).total <= limit) {
+            best.stages = st;
+            best.gp = panels;
+            return best;
+        }
+    int lead = 0;
+    for (int gp : {4, 2, 1}) {
+        if (gp >= panels || (gp == 1 && lead > 0)) continue;
+        for (int st = kMaxStages; st >= 2; --st)
+            if (smem_plan(kp, st, gp).total <= limit) {
+                if ((st - 1) * gp > lead) {
+                    lead = (st - 1) * gp;
+                    best.stages = st;
+                    best.gp = gp;
+                }
+                break;
+            }
+    }
+    return best;
 }
 
 // ------------------------------------------------------------------ schedule
@@ -351,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    const Smem P = smem_plan(a.kp, a.stages);
+    const Smem P = smem_plan(a.kp, a.stages, a.gp);
     const int panels = a.kp / 8;
     const int S = a.stages;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P.bars);
@@ -439,12 +469,18 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                         tw[0] += c1 - c0;
                         c0 = c1;
                     }
-                    const int s = g % S;
-                    if (!mbar_wait(&r_empty[s], ((g / S) & 1) ^ 1, abort_flag, a.err, 2)) { ok = false; break; }
+                    // the row block in ng stages of gp panels (one stage when a whole block fits)
+                    const unsigned char* rsrc = a.aimg + (size_t)t.X * blk_bytes;
+                    for (int q = 0; q < a.ng; ++q) {
+                        const int s = g % S;
+                        if (!mbar_wait(&r_empty[s], ((g / S) & 1) ^ 1, abort_flag, a.err, 2)) { ok = false; break; }
+                        const uint32_t bytes = (uint32_t)min(a.gp, panels - q * a.gp) * (kRows * 32);
+                        mbar_expect_tx(&r_full[s], bytes);
+                        bulk_load(sm + P.rows[s], rsrc + (size_t)q * a.gp * (kRows * 32), bytes, &r_full[s]);
+                        ++g;
+                    }
                     tw[1] += clock64() - c0;
-                    mbar_expect_tx(&r_full[s], blk_bytes);
-                    bulk_load(sm + P.rows[s], a.aimg + (size_t)t.X * blk_bytes, blk_bytes, &r_full[s]);
-                    ++g;
+                    if (!ok) break;
                 }
                 if (have) ++ti;
             }
@@ -474,11 +510,11 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
         if (lane == 0) {
             int g = 0, ti = 0, s = 0;
             uint32_t rph = 0;   // parity of the next row-stage fill
-            bool ok = true;
+            bool ok = true, issued = false;
             const long long t_start = clock64();
             const uint64_t cdesc = sw32_desc(su32(sm + P.cols));
             const uint64_t rdesc0 = sw32_desc(su32(sm + P.rows[0]));
-            const uint64_t rstride = (uint64_t)(blk_bytes >> 4);   // one row stage in descriptor units
+            const uint64_t rstride = (uint64_t)((a.gp * kRows * 32) >> 4);   // one row stage in descriptor units
             for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
                 int rho, Y, p_lo;
                 const int nu = item_span(a, item, rho, Y, p_lo);
@@ -491,21 +527,27 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                         have = true;
                     }
                     const int acc = g & 1;
-                    if (!mbar_wait_fast(&r_full[s], rph, abort_flag, a.err, 4)) { ok = false; break; }
                     if (!mbar_wait_fast(&acc_empty[acc], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 5)) { ok = false; break; }
-                    tc_fence_after();
                     const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kCols);
-                    const uint64_t ad = rdesc0 + (uint64_t)s * rstride;
-                    for (int p = 0; p < panels; ++p)
-                        mma_tf32(d_tmem, ad + (uint64_t)(p * ((kRows * 32) >> 4)), cdesc + (uint64_t)(p * ((kCols * 32) >> 4)),
-                                 p > 0 ? 1u : 0u);
-                    mma_commit(&r_empty[s]);
+                    int p = 0;   // K panel of the tile
+                    for (int q = 0; q < a.ng; ++q) {
+                        if (!mbar_wait_fast(&r_full[s], rph, abort_flag, a.err, 4)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint64_t ad = rdesc0 + (uint64_t)s * rstride;
+                        const int pe = min(p + a.gp, panels);
+                        for (int pq = 0; p < pe; ++p, ++pq)
+                            mma_tf32(d_tmem, ad + (uint64_t)(pq * ((kRows * 32) >> 4)),
+                                     cdesc + (uint64_t)(p * ((kCols * 32) >> 4)), p > 0 ? 1u : 0u);
+                        issued = true;
+                        mma_commit(&r_empty[s]);
+                        if (++s == S) {
+                            s = 0;
+                            rph ^= 1;
+                        }
+                    }
+                    if (!ok) break;
                     mma_commit(&acc_full[acc]);
                     ++g;
-                    if (++s == S) {
-                        s = 0;
-                        rph ^= 1;
-                    }
                 }
                 if (have && ok) {
                     mma_commit(c_empty);
@@ -513,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                 }
             }
             // on abort, wait (bounded) until the MMAs already issued have finished with TMEM
-            if (!ok && g > 0) {
+            if (!ok && issued) {
                 mma_commit(drain);
                 const long long t0 = clock64();
                 while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) {
@@ -767,7 +809,7 @@ __global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, i
 namespace {
 
 struct TcState {
-    int n = 0, d = 0, kp = 0, dp = 0, npad = 0, sms = 0, stages = 0;
+    int n = 0, d = 0, kp = 0, dp = 0, npad = 0, sms = 0, stages = 0, gp = 0;
     unsigned char *A = nullptr, *B = nullptr;
     float *xp = nullptr, *ntf = nullptr;
     float* nrm = nullptr;   // nrm / thr belong to the scheduler
@@ -795,7 +837,7 @@ bool tc_engine_supported(int d)
         if (dev < 64) cc[dev].store(v);
     }
     const int kp = tc_kp(d);
-    return v == 100 && kp <= tc::kMaxKp && tc::pick_stages(kp) > 0;
+    return v == 100 && tc::pick_plan(kp).stages > 0;
 }
 
 // Prepares the TF32 operand images, the TF32 norms and the point-major original coordinates for
@@ -832,7 +874,9 @@ TcFold tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const fl
     st.kp = kp;
     st.dp = dp;
     st.npad = npad;
-    st.stages = tc::pick_stages(kp);
+    const tc::StagePlan plan = tc::pick_plan(kp);
+    st.stages = plan.stages;
+    st.gp = plan.gp;
     (void)U;   // the folded bounds live in the row image; the scheduler keeps V for its own use
     st.nrm = const_cast<float*>(norms);
     st.thr = const_cast<uint64_t*>(thr);
@@ -853,6 +897,8 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.dp = st.dp;
     a.T = r.T;
     a.stages = st.stages;
+    a.gp = st.gp;
+    a.ng = (st.kp / 8 + st.gp - 1) / st.gp;
     a.cap = r.cap;
     a.exact = precision == FDB200_FP32 ? 1 : 0;
     a.diag = r.diag;
@@ -892,12 +938,15 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
         a.items = T * (a.nchunk0 + (a.np[1] + ppi - 1) / ppi);
     }
     if (a.items <= 0 || r.nb <= 0) return;
-    const tc::Smem P = tc::smem_plan(st.kp, st.stages);
+    const tc::Smem P = tc::smem_plan(st.kp, st.stages, st.gp);
     const size_t smem = P.total + 1024;
-    static bool attr_set = false;
-    if (!attr_set) {
+    // the shared-memory opt-in is a per-device function attribute
+    static std::atomic<bool> attr_set[64] = {};
+    int dev = 0;
+    FDB_CUDA(cudaGetDevice(&dev));
+    if (dev >= 64 || !attr_set[dev].load()) {
         FDB_CUDA(cudaFuncSetAttribute(tc::knn_tile_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        attr_set = true;
+        if (dev < 64) attr_set[dev].store(true);
     }
     const int grid = std::min(a.items, st.sms);
     tc::knn_tile_tc<<<grid, tc::kThreads, smem, s>>>(a);

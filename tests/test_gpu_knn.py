@@ -33,7 +33,7 @@ def test_spiral_knn_bit_exact(fdb, oracle, spiral_dm):
 def test_random_shapes_bit_exact(fdb, oracle, n, d, k, engine):
     rng = np.random.default_rng(n * 131 + d)
     x = rng.uniform(-1, 1, (d, n)).astype(np.float32)
-    _check_equal(fdb, oracle, x, k, engine=engine if d <= 50 else "simt")
+    _check_equal(fdb, oracle, x, k, engine=engine)
 
 
 @pytest.mark.parametrize("k", [1, 8, 64, 200])

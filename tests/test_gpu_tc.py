@@ -78,3 +78,43 @@ def test_auto_engine_mixes_rounds_and_stays_exact(fdb):
     b = fdb.knn(x, 45, engine="tcgen05")
     assert a[2]["engine_used"] == 2 and a[2]["rounds"] == b[2]["rounds"]
     assert np.array_equal(a[1], b[1]) and np.array_equal(a[0], b[0])
+
+
+@pytest.mark.parametrize("d", [59, 78, 100, 128, 150])
+def test_tc_large_dimensions_bit_exact(fdb, oracle, d):
+    """K = d + 6 padded to 8. Up to K = 80 two whole row blocks are staged beside the resident column
+    pair; beyond that a row stage holds a group of K panels (4 panels at d = 78, 2 at d = 100 and 128,
+    1 at d = 150) and a tile takes several stages. The lists stay bit-exact."""
+    rng = np.random.default_rng(d)
+    x = rng.uniform(-1, 1, (d, 3000)).astype(np.float32)
+    _exact(fdb, oracle, x, 20)
+
+
+def test_tc_scale_out_mixture_sample(fdb, oracle):
+    # the 128-dimensional scale-out mixture (k = 64) at a size the oracle finishes in seconds
+    _exact(fdb, oracle, ds.scale_out(n=12000, d=128, seed=4), 64)
+
+
+def test_tc_matches_simt_at_128_dimensions(fdb):
+    x = ds.scale_out(n=60000, d=128, seed=6)
+    a = fdb.knn(x, 64, engine="tcgen05")
+    b = fdb.knn(x, 64, engine="simt")
+    assert np.array_equal(a[1], b[1]) and np.array_equal(a[0], b[0])
+
+
+def test_tf32_mode_at_128_dimensions_close(fdb, oracle):
+    x = ds.scale_out(n=6000, d=128, seed=7)
+    dist, idx, st = fdb.knn(x, 64, engine="tcgen05", precision="tf32")
+    assert st["engine_used"] == 2
+    nrm = oracle.norms(x)
+    xc = np.ascontiguousarray(x)
+    for i in range(0, 6000, 211):
+        for q in range(0, 64, 7):
+            j = int(idx[q, i])
+            exact_d2 = oracle.lib().or_pair_d2(xc, 6000, 128, nrm, i, j)
+            bound = 2 ** -8 * 1.01 * np.sqrt(nrm[i] * nrm[j]) + 1e-4 * (nrm[i] + nrm[j])
+            assert abs(float(dist[q, i]) ** 2 - exact_d2) <= bound
+    od, oi = oracle.knn(x, 64)
+    recall = np.mean([len(set(idx[:, i]) & set(oi[:, i])) / 64 for i in range(6000)])
+    assert recall > 0.95
+    assert (np.diff(dist, axis=0) >= 0).all()
