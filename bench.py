@@ -40,6 +40,17 @@ PUBLISHED_A6000_FIT_S = 16.49          # README.md:149, symwarp FP32 Fit seconds
 # was taken on the full workload.
 TILE_DRAM_BYTES_PER_FIT = 366.15e9
 WORKLOAD = dict(n=1_291_147, d=50, k=45, c=20)
+# the synthetic configurations (fastdec_b200.datasets): the headline GloVe-like cloud, the 100k GMM and
+# the 4M x 128 scale-out mixture; --n/--d/--k/--c override a configuration's shape
+CONFIGS = {
+    "glove_like": dict(WORKLOAD, gen="embedding_cloud",
+                       note="seeded stand-in for GloVe 50d (20 anisotropic Gaussians, Zipf(1.1) weights, "
+                            "5% Student-t(3) points, min-max scaled to [-1,1])"),
+    "gmm100k": dict(n=100_000, d=16, k=20, c=10, gen="gmm_isotropic",
+                    note="10 isotropic Gaussians, centers U[-10,10]^16, sigma 1"),
+    "scale_out": dict(n=4_000_000, d=128, k=64, c=50, gen="scale_out",
+                      note="50 rotated anisotropic Gaussians (per-axis sigma log-U[0.1,1]), min-max scaled to [-1,1]"),
+}
 
 
 def parse():
@@ -48,10 +59,11 @@ def parse():
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--n", type=int, default=WORKLOAD["n"])
-    p.add_argument("--d", type=int, default=WORKLOAD["d"])
-    p.add_argument("--k", type=int, default=WORKLOAD["k"])
-    p.add_argument("--c", type=int, default=WORKLOAD["c"])
+    p.add_argument("--config", default="glove_like", choices=sorted(CONFIGS))
+    p.add_argument("--n", type=int, default=None)
+    p.add_argument("--d", type=int, default=None)
+    p.add_argument("--k", type=int, default=None)
+    p.add_argument("--c", type=int, default=None)
     p.add_argument("--precision", default="fp32", choices=["fp32", "tf32"])
     p.add_argument("--density", default="laplacian", choices=["laplacian", "gaussian"])
     p.add_argument("--engine", default="auto", choices=["auto", "simt", "tcgen05"])
@@ -59,12 +71,27 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=8.0, help="target CPU seconds per reference sample")
-    return p.parse_args()
+    a = p.parse_args()
+    for key in ("n", "d", "k", "c"):
+        if getattr(a, key) is None:
+            setattr(a, key, CONFIGS[a.config][key])
+    return a
 
 
 def dataset(a):
-    from fastdec_b200.datasets import embedding_cloud
-    return embedding_cloud(n=a.n, d=a.d, seed=a.seed)
+    import fastdec_b200.datasets as ds
+    return getattr(ds, CONFIGS[a.config]["gen"])(n=a.n, d=a.d, seed=a.seed)
+
+
+def data_note(a):
+    return "synthetic: " + CONFIGS[a.config]["note"]
+
+
+def vs_baseline(a, value):
+    """value / the published pairs/s of the reference's GloVe 50d Fit; only for that shape"""
+    if (a.config, a.n, a.d, a.k, a.c) != ("glove_like", WORKLOAD["n"], WORKLOAD["d"], WORKLOAD["k"], WORKLOAD["c"]):
+        return None
+    return value / (pairs_of(WORKLOAD["n"]) / PUBLISHED_A6000_FIT_S)
 
 
 _T0 = time.time()
@@ -85,18 +112,18 @@ def pairs_of(n):
 
 
 def config_of(a, extra=None):
-    c = {"workload": f"glove_like {a.n:,} x {a.d}, k={a.k}, c={a.c}, {a.precision.upper()} distances, "
+    mb = lambda b: f"{b / 1e6:,.0f} MB"
+    c = {"workload": f"{a.config} {a.n:,} x {a.d}, k={a.k}, c={a.c}, {a.precision.upper()} distances, "
                      f"{a.density} density",
          "n": a.n, "d": a.d, "k": a.k, "c": a.c, "precision": a.precision, "density": a.density,
          "engine": a.engine, "seed": a.seed, "parallelism": f"triangle-sharded x{a.gpus}",
-         "l2": "inputs larger than L2 (258 MB dataset, 465 MB lists per fit; no flush needed)"}
+         "l2": f"inputs larger than L2 ({mb(4 * a.n * a.d)} dataset, {mb(8 * a.n * a.k)} lists per fit; "
+               "no flush needed)" if 8 * a.n * a.k > 126e6 else "inputs smaller than L2 (not flushed)"}
     if extra:
         c.update(extra)
     return c
 
 
-DATA_NOTE = ("synthetic: seeded stand-in for GloVe 50d (20 anisotropic Gaussians, Zipf(1.1) weights, "
-             "5% Student-t(3) points, min-max scaled to [-1,1])")
 
 
 # ------------------------------------------------------------------ clocks during the timed region
@@ -215,8 +242,8 @@ def main():
         out = {"impl": "reference", "metric": "fit_distance_pairs_per_s", "value": ref["value"], "unit": "pairs/s",
                "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ref["seconds_per_fit"] * 1e3,
                "higher_is_better": True, "scaling": "strong",
-               "vs_baseline": ref["value"] / (pairs_of(WORKLOAD["n"]) / PUBLISHED_A6000_FIT_S),
-               "dtype": "f32", "data": DATA_NOTE, "config": config_of(a, {"sample_points": ref["n_sample"]}),
+               "vs_baseline": vs_baseline(a, ref["value"]),
+               "dtype": "f32", "data": data_note(a), "config": config_of(a, {"sample_points": ref["n_sample"]}),
                "cpu_baseline": {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
                "e2e": {"value": ref["value"], "unit": "pairs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(out), flush=True)
@@ -347,7 +374,7 @@ def main():
     tf32_peak = bf16 / 2.0
     flops = shard_pairs * 2 * d
     achieved = flops / (tile_ms / 1e3) / 1e12 if tile_ms > 0 else None
-    default_shape = (n, d, k, world, a.precision) == (WORKLOAD["n"], WORKLOAD["d"], WORKLOAD["k"], 1, "fp32")
+    default_shape = vs_baseline(a, 1.0) is not None and (world, a.precision, a.engine) == (1, "fp32", "auto")
     kp = ((d + 6 + 7) // 8) * 8
     roofline = {"bound": "tensor", "kernel": "distance tiles (knn_tile_simt for the dense first rounds + knn_tile_tc, all rounds of a fit)",
                 "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
@@ -359,12 +386,13 @@ def main():
                 "algorithmic_note": "N(N-1)/2 pairs x 2d FLOPs (the reference's -2 X X^T GEMM work)",
                 "tensor_flops_per_fit": float(n) * n * kp * 2 if engine_name(stats) == "tcgen05" else None,
                 "tensor_note": "upper bound of what the tcgen05 pipe executes: every ordered pair, K = d + 6 padded "
-                                "to 8 (the rounds the automatic engine gives the SIMT tiles cover 0.4 % of the pairs)"}
+                                "to 8 (the first rounds, which the automatic engine gives the SIMT tiles, cover 0.4 % of "
+                                "the pairs at the headline shape)"}
     last = stats[-1]
     out = {"metric": "fit_distance_pairs_per_s", "value": value, "unit": "pairs/s", "n_gpus": world,
            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-           "scaling": "strong", "vs_baseline": value / (pairs_of(WORKLOAD["n"]) / PUBLISHED_A6000_FIT_S),
-           "dtype": "f32" if a.precision == "fp32" else "tf32", "data": DATA_NOTE, "config": config_of(a),
+           "scaling": "strong", "vs_baseline": vs_baseline(a, value),
+           "dtype": "f32" if a.precision == "fp32" else "tf32", "data": data_note(a), "config": config_of(a),
            "fit_s": ms_step / 1e3, "knn_s": last.get("knn_ms", 0) / 1e3,
            "stages_ms": {k2: last.get(k2) for k2 in ("knn_ms", "knn_tile_ms", "density_ms", "dc_ms", "labels_ms")},
            "rounds": last.get("rounds"), "admitted_candidates": last.get("candidates"),

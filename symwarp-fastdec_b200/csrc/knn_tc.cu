@@ -228,7 +228,7 @@ __device__ __forceinline__ void tmem_wait(uint32_t (&r)[32])
 // ------------------------------------------------------------------ shared memory plan
 struct Smem {
     // offsets in bytes from the 1024-aligned base
-    uint32_t cols, rows[kMaxStages], queue, qcount, raw, bars, misc, total;
+    uint32_t cols, rows, rstage, queue, qcount, raw, bars, misc, total;   // row stage q at rows + q * rstage
 };
 
 __host__ __device__ inline Smem smem_plan(int kp, int stages, int gp)
@@ -238,10 +238,9 @@ __host__ __device__ inline Smem smem_plan(int kp, int stages, int gp)
     uint32_t o = 0;
     s.cols = o;                        // panel p: column block Y (4 KB) then Y + 1 (4 KB)
     o += panels * kCols * 32;
-    for (int q = 0; q < kMaxStages; ++q) {
-        s.rows[q] = o;                 // gp panels of one row block
-        if (q < stages) o += (uint32_t)gp * kRows * 32;
-    }
+    s.rows = o;                        // stages x (gp panels of one row block)
+    s.rstage = (uint32_t)gp * kRows * 32;
+    o += (uint32_t)stages * s.rstage;
     s.queue = o;                       // per queue: rows[cap], first columns[cap], masks[cap]; filter
     o += (uint32_t)kQueues * kQueueCap * 12u;   // warp e owns entries [e * kSlots, (e + 1) * kSlots)
     s.qcount = o;                      // per queue and filter warp: entries written
@@ -377,6 +376,9 @@ __device__ __forceinline__ void settle_row(const Args& a, int gi, int gj0, unsig
 }
 
 // ------------------------------------------------------------------ the kernel
+// kSplitK: row blocks arrive in several stages of gp K panels (large K); otherwise one stage holds a
+// whole row block and the producer and MMA loops keep their single-stage form
+template <bool kSplitK>
 __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -469,18 +471,27 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                         tw[0] += c1 - c0;
                         c0 = c1;
                     }
-                    // the row block in ng stages of gp panels (one stage when a whole block fits)
                     const unsigned char* rsrc = a.aimg + (size_t)t.X * blk_bytes;
-                    for (int q = 0; q < a.ng; ++q) {
+                    if constexpr (kSplitK) {
+                        // the row block in ng stages of gp panels
+                        for (int q = 0; q < a.ng; ++q) {
+                            const int s = g % S;
+                            if (!mbar_wait(&r_empty[s], ((g / S) & 1) ^ 1, abort_flag, a.err, 2)) { ok = false; break; }
+                            const uint32_t bytes = (uint32_t)min(a.gp, panels - q * a.gp) * (kRows * 32);
+                            mbar_expect_tx(&r_full[s], bytes);
+                            bulk_load(sm + P.rows + s * P.rstage, rsrc + (size_t)q * a.gp * (kRows * 32), bytes, &r_full[s]);
+                            ++g;
+                        }
+                        tw[1] += clock64() - c0;
+                        if (!ok) break;
+                    } else {
                         const int s = g % S;
                         if (!mbar_wait(&r_empty[s], ((g / S) & 1) ^ 1, abort_flag, a.err, 2)) { ok = false; break; }
-                        const uint32_t bytes = (uint32_t)min(a.gp, panels - q * a.gp) * (kRows * 32);
-                        mbar_expect_tx(&r_full[s], bytes);
-                        bulk_load(sm + P.rows[s], rsrc + (size_t)q * a.gp * (kRows * 32), bytes, &r_full[s]);
+                        tw[1] += clock64() - c0;
+                        mbar_expect_tx(&r_full[s], blk_bytes);
+                        bulk_load(sm + P.rows + s * P.rstage, rsrc, blk_bytes, &r_full[s]);
                         ++g;
                     }
-                    tw[1] += clock64() - c0;
-                    if (!ok) break;
                 }
                 if (have) ++ti;
             }
@@ -513,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
             bool ok = true, issued = false;
             const long long t_start = clock64();
             const uint64_t cdesc = sw32_desc(su32(sm + P.cols));
-            const uint64_t rdesc0 = sw32_desc(su32(sm + P.rows[0]));
+            const uint64_t rdesc0 = sw32_desc(su32(sm + P.rows));
             const uint64_t rstride = (uint64_t)((a.gp * kRows * 32) >> 4);   // one row stage in descriptor units
             for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
                 int rho, Y, p_lo;
@@ -527,16 +538,33 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                         have = true;
                     }
                     const int acc = g & 1;
-                    if (!mbar_wait_fast(&acc_empty[acc], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 5)) { ok = false; break; }
                     const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kCols);
-                    int p = 0;   // K panel of the tile
-                    for (int q = 0; q < a.ng; ++q) {
+                    if constexpr (kSplitK) {
+                        if (!mbar_wait_fast(&acc_empty[acc], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 5)) { ok = false; break; }
+                        int p = 0;   // K panel of the tile
+                        for (int q = 0; q < a.ng; ++q) {
+                            if (!mbar_wait_fast(&r_full[s], rph, abort_flag, a.err, 4)) { ok = false; break; }
+                            tc_fence_after();
+                            const uint64_t ad = rdesc0 + (uint64_t)s * rstride;
+                            const int pe = min(p + a.gp, panels);
+                            for (int pq = 0; p < pe; ++p, ++pq)
+                                mma_tf32(d_tmem, ad + (uint64_t)(pq * ((kRows * 32) >> 4)),
+                                         cdesc + (uint64_t)(p * ((kCols * 32) >> 4)), p > 0 ? 1u : 0u);
+                            issued = true;
+                            mma_commit(&r_empty[s]);
+                            if (++s == S) {
+                                s = 0;
+                                rph ^= 1;
+                            }
+                        }
+                        if (!ok) break;
+                    } else {
                         if (!mbar_wait_fast(&r_full[s], rph, abort_flag, a.err, 4)) { ok = false; break; }
+                        if (!mbar_wait_fast(&acc_empty[acc], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 5)) { ok = false; break; }
                         tc_fence_after();
                         const uint64_t ad = rdesc0 + (uint64_t)s * rstride;
-                        const int pe = min(p + a.gp, panels);
-                        for (int pq = 0; p < pe; ++p, ++pq)
-                            mma_tf32(d_tmem, ad + (uint64_t)(pq * ((kRows * 32) >> 4)),
+                        for (int p = 0; p < panels; ++p)
+                            mma_tf32(d_tmem, ad + (uint64_t)(p * ((kRows * 32) >> 4)),
                                      cdesc + (uint64_t)(p * ((kCols * 32) >> 4)), p > 0 ? 1u : 0u);
                         issued = true;
                         mma_commit(&r_empty[s]);
@@ -545,7 +573,6 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                             rph ^= 1;
                         }
                     }
-                    if (!ok) break;
                     mma_commit(&acc_full[acc]);
                     ++g;
                 }
@@ -945,11 +972,13 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     int dev = 0;
     FDB_CUDA(cudaGetDevice(&dev));
     if (dev >= 64 || !attr_set[dev].load()) {
-        FDB_CUDA(cudaFuncSetAttribute(tc::knn_tile_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        FDB_CUDA(cudaFuncSetAttribute(tc::knn_tile_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        FDB_CUDA(cudaFuncSetAttribute(tc::knn_tile_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         if (dev < 64) attr_set[dev].store(true);
     }
     const int grid = std::min(a.items, st.sms);
-    tc::knn_tile_tc<<<grid, tc::kThreads, smem, s>>>(a);
+    if (a.ng > 1) tc::knn_tile_tc<true><<<grid, tc::kThreads, smem, s>>>(a);
+    else tc::knn_tile_tc<false><<<grid, tc::kThreads, smem, s>>>(a);
     FDB_LAUNCHED();
 }
 
