@@ -46,7 +46,7 @@ typedef struct FdB200Opts {
                                  (fmaf chain); FDB200_TF32: tensor-core TF32 distances */
     int density_kernel;       /* FDB200_LAPLACIAN (default) or FDB200_GAUSSIAN */
     int engine;               /* which distance-tile engine runs the self-kNN: AUTO = tcgen05 where
-                                 supported (sm_100 and d <= 154), with the first (dense) rounds on
+                                 supported (sm_100 and d <= 178), with the first (dense) rounds on
                                  the exact SIMT tiles; TCGEN05 = tcgen05 for every round; SIMT =
                                  SIMT for every round (any d; FP32 only) */
     int inputs_on_device;     /* nonzero: data / density / index inputs are device pointers */

@@ -61,9 +61,15 @@ constexpr int kRows = 128;               // rows per tile (one block)
 constexpr int kCols = 256;               // columns per tile (two blocks)
 constexpr int kMaxStages = 8;            // row stages in shared memory
 constexpr int kQueues = 8;               // survivor queues between filter and refine warps
-constexpr int kQueueCap = 256;           // entries per queue
-constexpr int kSlots = kQueueCap / kFilterWarps;   // a filter warp's share of one queue
-constexpr int kRawPerWarp = 4;           // survivor rows a filter warp may park raw per tile
+// survivor queue entries and parked raw rows per filter warp and tile. The split-K shape (large K)
+// gives half of both to row stages: its MMA takes over 2,000 cycles a tile, so the filter has slack,
+// and larger row stages mean fewer of them per tile.
+template <bool kSplitK>
+struct QueueShape {
+    static constexpr int cap = kSplitK ? 128 : 256;      // entries per queue
+    static constexpr int slots = cap / kFilterWarps;      // a filter warp's share of one queue
+    static constexpr int raw = kSplitK ? 2 : 4;           // survivor rows a filter warp may park raw
+};
 constexpr int kMaxKp = 256;              // K bound; what fits in shared memory decides (pick_plan)
 constexpr long long kWaitCycles = 2000000000ll;   // ~1 s at 2 GHz
 constexpr float kPoisonNorm = 1.2676506002282294e30f;   // 2^100, exact in TF32
@@ -231,8 +237,10 @@ struct Smem {
     uint32_t cols, rows, rstage, queue, qcount, raw, bars, misc, total;   // row stage q at rows + q * rstage
 };
 
-__host__ __device__ inline Smem smem_plan(int kp, int stages, int gp)
+__host__ __device__ inline Smem smem_plan(int kp, int stages, int gp, bool split)
 {
+    const uint32_t qcap = split ? QueueShape<true>::cap : QueueShape<false>::cap;
+    const uint32_t raw = split ? QueueShape<true>::raw : QueueShape<false>::raw;
     Smem s;
     const uint32_t panels = (uint32_t)kp / 8;
     uint32_t o = 0;
@@ -242,12 +250,12 @@ __host__ __device__ inline Smem smem_plan(int kp, int stages, int gp)
     s.rstage = (uint32_t)gp * kRows * 32;
     o += (uint32_t)stages * s.rstage;
     s.queue = o;                       // per queue: rows[cap], first columns[cap], masks[cap]; filter
-    o += (uint32_t)kQueues * kQueueCap * 12u;   // warp e owns entries [e * kSlots, (e + 1) * kSlots)
+    o += (uint32_t)kQueues * qcap * 12u;        // warp e owns entries [e * slots, (e + 1) * slots)
     s.qcount = o;                      // per queue and filter warp: entries written
     o += kQueues * kFilterWarps * 4;
     o = (o + 15) & ~15u;
-    s.raw = o;                         // per queue and filter warp: kRawPerWarp rows of 32 words
-    o += (uint32_t)kQueues * kFilterWarps * kRawPerWarp * 128u;
+    s.raw = o;                         // per queue and filter warp: raw rows of 32 words
+    o += (uint32_t)kQueues * kFilterWarps * raw * 128u;
     s.bars = o;
     o += 48 * 8;
     s.misc = o;
@@ -261,10 +269,12 @@ struct StagePlan {
 };
 
 // How row blocks are staged. While two or more whole row blocks fit next to the resident column
-// pair (K <= 72), a stage holds one block (up to 4 stages) and every tile is one stage. For larger
+// pair (K <= 80), a stage holds one block (up to 4 stages) and every tile is one stage. For larger
 // K the column pair takes most of the 227 KB a CTA may use, so a stage holds gp consecutive K panels
-// of a block and a tile takes ceil(panels / gp) stages; the plan with the most panels in flight
-// ahead of the MMA wins, single-panel stages (twice the barrier traffic) only when no other fits.
+// of a block and a tile takes ng = ceil(panels / gp) stages. Each stage of a tile costs the tensor
+// pipe a fixed overhead on top of its MMAs (measured at 1M x 128, K = 136, late rounds: 6,120 cycles
+// a tile with 2-panel stages, 4,420 with 4, 3,840 with 6; the MMAs alone take 2,176), so the plan
+// takes the fewest stages per tile that fit, with as many stages in flight as fit.
 inline StagePlan pick_plan(int kp)
 {
     const uint32_t limit = 227u * 1024u - 1024u;
@@ -272,22 +282,18 @@ inline StagePlan pick_plan(int kp)
     StagePlan best;
     if (kp > kMaxKp || kp % 8) return best;
     for (int st = 4; st >= 2; --st)
-        if (smem_plan(kp, st, panels).total <= limit) {
+        if (smem_plan(kp, st, panels, false).total <= limit) {
             best.stages = st;
             best.gp = panels;
             return best;
         }
-    int lead = 0;
-    for (int gp : {4, 2, 1}) {
-        if (gp >= panels || (gp == 1 && lead > 0)) continue;
+    for (int ng = 2; ng <= panels; ++ng) {
+        const int gp = (panels + ng - 1) / ng;
         for (int st = kMaxStages; st >= 2; --st)
-            if (smem_plan(kp, st, gp).total <= limit) {
-                if ((st - 1) * gp > lead) {
-                    lead = (st - 1) * gp;
-                    best.stages = st;
-                    best.gp = gp;
-                }
-                break;
+            if (smem_plan(kp, st, gp, true).total <= limit) {
+                best.stages = st;
+                best.gp = gp;
+                return best;
             }
     }
     return best;
@@ -383,7 +389,10 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    const Smem P = smem_plan(a.kp, a.stages, a.gp);
+    const Smem P = smem_plan(a.kp, a.stages, a.gp, kSplitK);
+    constexpr int kQueueCap = QueueShape<kSplitK>::cap;
+    constexpr int kSlots = QueueShape<kSplitK>::slots;
+    constexpr int kRawPerWarp = QueueShape<kSplitK>::raw;
     const int panels = a.kp / 8;
     const int S = a.stages;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P.bars);
@@ -965,7 +974,7 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
         a.items = T * (a.nchunk0 + (a.np[1] + ppi - 1) / ppi);
     }
     if (a.items <= 0 || r.nb <= 0) return;
-    const tc::Smem P = tc::smem_plan(st.kp, st.stages, st.gp);
+    const tc::Smem P = tc::smem_plan(st.kp, st.stages, st.gp, a.ng > 1);
     const size_t smem = P.total + 1024;
     // the shared-memory opt-in is a per-device function attribute
     static std::atomic<bool> attr_set[64] = {};

@@ -80,11 +80,12 @@ def test_auto_engine_mixes_rounds_and_stays_exact(fdb):
     assert np.array_equal(a[1], b[1]) and np.array_equal(a[0], b[0])
 
 
-@pytest.mark.parametrize("d", [59, 78, 100, 128, 150])
+@pytest.mark.parametrize("d", [59, 78, 100, 128, 150, 178])
 def test_tc_large_dimensions_bit_exact(fdb, oracle, d):
     """K = d + 6 padded to 8. Up to K = 80 two whole row blocks are staged beside the resident column
-    pair; beyond that a row stage holds a group of K panels (4 panels at d = 78, 2 at d = 100 and 128,
-    1 at d = 150) and a tile takes several stages. The lists stay bit-exact."""
+    pair; beyond that a row stage holds a group of K panels (6 of 11 at d = 78, 7 of 14 at d = 100,
+    6 of 17 at d = 128, 4 of 20 at d = 150, 1 of 23 at d = 178, the largest K that fits) and a tile
+    takes several stages. The lists stay bit-exact."""
     rng = np.random.default_rng(d)
     x = rng.uniform(-1, 1, (d, 3000)).astype(np.float32)
     _exact(fdb, oracle, x, 20)
