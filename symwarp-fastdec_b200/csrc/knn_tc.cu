@@ -81,6 +81,7 @@ struct Args {
     int b_lo, nb;                // row blocks of this shard
     int r0[2], len[2], np[2];    // forward / backward offset ranges: first offset, length, pairs
     int ppi, nchunk0, items;     // pairs per work item, items of the forward range, all items
+    int ywin;                    // column blocks per offset chunk: T, or the window a shard's rows reach
     const float* nrm;            // exact fp32 norms
     const uint64_t* thr;         // exact admission thresholds
     const float* xp;             // original coordinates, point-major, dp floats per row
@@ -310,10 +311,18 @@ __device__ __forceinline__ int item_span(const Args& a, int item, int& rho, int&
         p_lo = 0;
         return 1;
     }
-    const int gc = item / a.T;
-    Y = item - gc * a.T;
+    const int gc = item / a.ywin;
+    const int w = item - gc * a.ywin;
     rho = gc < a.nchunk0 ? 0 : 1;
     p_lo = (rho ? gc - a.nchunk0 : gc) * a.ppi;
+    if (a.ywin == a.T) {
+        Y = w;
+    } else {
+        // a shard: only the column blocks Y whose rows X = Y - delta (delta = r0 + 2p over the chunk)
+        // can fall in the shard's row blocks
+        Y = a.b_lo + a.r0[rho] + 2 * p_lo + w;
+        Y %= a.T;
+    }
     return min(a.np[rho], p_lo + a.ppi) - p_lo;
 }
 
@@ -964,14 +973,17 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
         a.len[1] = L - e;
         a.np[0] = (a.len[0] + 1) / 2;
         a.np[1] = (a.len[1] + 1) / 2;
-        // about 8 items per CTA so the tail of a round stays short
+        // about 8 items of real tiles per CTA so the tail of a round stays short
         const long long want_items = 8ll * st.sms;
-        const long long pairs = (long long)T * (a.np[0] + a.np[1]);
+        const long long pairs = (long long)r.nb * (a.np[0] + a.np[1]);
         int ppi = (int)std::max<long long>(1, (pairs + want_items - 1) / want_items);
         ppi = std::min(ppi, std::max(a.np[0], 1));
         a.ppi = ppi;
         a.nchunk0 = (a.np[0] + ppi - 1) / ppi;
-        a.items = T * (a.nchunk0 + (a.np[1] + ppi - 1) / ppi);
+        // a shard's rows X in [b_lo, b_lo + nb) meet, for one chunk of ppi offset pairs, the column
+        // blocks Y = X + delta: a window of nb + 2 ppi - 1 blocks (all T when unsharded)
+        a.ywin = (r.nb == T) ? T : std::min(T, r.nb + 2 * ppi - 1);
+        a.items = a.ywin * (a.nchunk0 + (a.np[1] + ppi - 1) / ppi);
     }
     if (a.items <= 0 || r.nb <= 0) return;
     const tc::Smem P = tc::smem_plan(st.kp, st.stages, st.gp, a.ng > 1);
