@@ -191,7 +191,7 @@ __host__ __device__ inline int next_pow2(int v)
 // (fold_bound of the threshold plus the TF32 margin)
 __global__ void knn_merge_kernel(uint64_t* __restrict__ lists, uint64_t* __restrict__ thr,
                                  float* __restrict__ U, const float* __restrict__ norms,
-                                 const uint64_t* __restrict__ cand, int* __restrict__ cnt, int n,
+                                 const uint64_t* __restrict__ cand, int* __restrict__ cnt, int p0, int n,
                                  int k, int cap, int pw, int d, int kp, int exact,
                                  unsigned long long* __restrict__ admitted, unsigned char* __restrict__ aimg,
                                  const float* __restrict__ ntf, const int* __restrict__ stop)
@@ -199,7 +199,7 @@ __global__ void knn_merge_kernel(uint64_t* __restrict__ lists, uint64_t* __restr
     extern __shared__ uint64_t msm[];
     if (stop[0] | stop[1]) return;   // the round overflowed or an earlier one stopped: lists stay as they are
     const int warps = blockDim.x >> 5, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int p = blockIdx.x * warps + w;
+    const int p = p0 + blockIdx.x * warps + w;   // points [p0, n)
     if (p >= n) return;
     int c = cnt[p];
     if (c == 0) return;
@@ -313,7 +313,7 @@ constexpr int kSortedMergeWarps = 8;
 __global__ void __launch_bounds__(kSortedMergeWarps * 32)
     knn_merge_sorted_kernel(uint64_t* __restrict__ lists, uint64_t* __restrict__ thr, float* __restrict__ U,
                             const float* __restrict__ norms, const uint64_t* __restrict__ cand,
-                            int* __restrict__ cnt, int n, int k, int cap, int d, int kp, int exact,
+                            int* __restrict__ cnt, int p0, int n, int k, int cap, int d, int kp, int exact,
                             unsigned long long* __restrict__ admitted, unsigned char* __restrict__ aimg,
                             const float* __restrict__ ntf, const int* __restrict__ stop)
 {
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(kSortedMergeWarps * 32)
     __shared__ uint64_t sc_all[kSortedMergeWarps][512];
     if (stop[0] | stop[1]) return;   // the round overflowed or an earlier one stopped: lists stay as they are
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int p = blockIdx.x * kSortedMergeWarps + w;
+    const int p = p0 + blockIdx.x * kSortedMergeWarps + w;   // points [p0, n)
     if (p >= n) return;
     int c = cnt[p];
     if (c == 0) return;
@@ -611,12 +611,15 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
             launch_tile_round(r, pl.units, pl.engine, cfg.precision, s);
             FDB_CUDA(cudaEventRecord(ev.get(2 * slot + 1), s));
             if (trace) FDB_CUDA(cudaEventRecord(m0, s));
+            // a tcgen05 round appends only to this shard's rows; a SIMT round to any point
+            const int plo = pl.engine == FDB200_ENGINE_TCGEN05 ? b_lo * kBlock : 0;
+            const int phi = pl.engine == FDB200_ENGINE_TCGEN05 ? std::min(n, b_hi * kBlock) : n;
             if (k <= kSortedMergeMaxK && cap <= 512)
-                knn_merge_sorted_kernel<<<(n + kSortedMergeWarps - 1) / kSortedMergeWarps, kSortedMergeWarps * 32, 0, s>>>(
-                    lists, thr, U, norms, cand, cnt, n, k, cap, d, kp, exact, admitted, fold.aimg, fold.ntf, ovf);
+                knn_merge_sorted_kernel<<<(phi - plo + kSortedMergeWarps - 1) / kSortedMergeWarps, kSortedMergeWarps * 32, 0, s>>>(
+                    lists, thr, U, norms, cand, cnt, plo, phi, k, cap, d, kp, exact, admitted, fold.aimg, fold.ntf, ovf);
             else
-                knn_merge_kernel<<<(n + mwarps - 1) / mwarps, mwarps * 32, msmem, s>>>(
-                    lists, thr, U, norms, cand, cnt, n, k, cap, pw, d, kp, exact, admitted, fold.aimg, fold.ntf, ovf);
+                knn_merge_kernel<<<(phi - plo + mwarps - 1) / mwarps, mwarps * 32, msmem, s>>>(
+                    lists, thr, U, norms, cand, cnt, plo, phi, k, cap, pw, d, kp, exact, admitted, fold.aimg, fold.ntf, ovf);
             FDB_LAUNCHED();
             if (trace) FDB_CUDA(cudaEventRecord(m1, s));
             if (!diag_done) {
