@@ -861,7 +861,18 @@ struct TcState {
     uint64_t* thr = nullptr;
 };
 
-TcState g_state;   // the prepared operands of the current kNN call (one per process)
+// The prepared operands of the current kNN call, one slot per device: calls on one device are
+// serialised by that device's workspace lock, calls on different devices may run concurrently.
+constexpr int kMaxDevices = 64;
+TcState g_state[kMaxDevices];
+
+TcState& state_of_current_device()
+{
+    int dev = 0;
+    FDB_CUDA(cudaGetDevice(&dev));
+    FDB_REQUIRE(dev >= 0 && dev < kMaxDevices, "device ordinal out of range for the tcgen05 engine");
+    return g_state[dev];
+}
 
 }  // namespace
 
@@ -891,7 +902,7 @@ bool tc_engine_supported(int d)
 TcFold tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const float* norms, const float* U,
                   const uint64_t* thr, cudaStream_t s)
 {
-    TcState& st = g_state;
+    TcState& st = state_of_current_device();
     const int kp = tc_kp(d);
     const int dp = ((d + 3) / 4) * 4;
     const int T = (n + kBlock - 1) / kBlock;
@@ -934,7 +945,7 @@ TcFold tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const fl
 void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStream_t s)
 {
     (void)units;
-    TcState& st = g_state;
+    TcState& st = state_of_current_device();
     tc::Args a{};
     a.n = r.n;
     a.d = r.d;
