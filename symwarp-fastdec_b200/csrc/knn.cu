@@ -262,9 +262,10 @@ __device__ __forceinline__ void warp_sort_regs(uint64_t (&v)[E], int lane)
                 for (int e = 0; e < E; ++e) {
                     const uint64_t o = __shfl_xor_sync(0xffffffffu, v[e], lx);
                     const bool asc = ((lane * E + e) & size) == 0;
-                    const bool take_min = (lower == asc);
-                    const uint64_t mn = v[e] < o ? v[e] : o, mx = v[e] < o ? o : v[e];
-                    v[e] = take_min ? mn : mx;
+                    // keep the own key when it is the one this lane wants (the smaller one when
+                    // taking the minimum): one 64-bit compare and one select per key
+                    const bool keep = (v[e] < o) == (lower == asc);
+                    v[e] = keep ? v[e] : o;
                 }
             }
         }
@@ -310,7 +311,7 @@ __device__ __forceinline__ void merge_point_sorted(uint64_t* __restrict__ lists,
 constexpr int kSortedMergeMaxK = 256;
 constexpr int kSortedMergeWarps = 8;
 
-__global__ void __launch_bounds__(kSortedMergeWarps * 32)
+__global__ void __launch_bounds__(kSortedMergeWarps * 32, 4)
     knn_merge_sorted_kernel(uint64_t* __restrict__ lists, uint64_t* __restrict__ thr, float* __restrict__ U,
                             const float* __restrict__ norms, const uint64_t* __restrict__ cand,
                             int* __restrict__ cnt, int p0, int n, int k, int cap, int d, int kp, int exact,
