@@ -100,3 +100,41 @@ def test_block_ranges_follow_the_kernel_row_block_split():
             assert all(rng[i][1] == rng[i + 1][0] for i in range(world - 1))
             T = (n + 127) // 128
             assert all(a == min(n, 128 * (T * r // world)) for r, (a, _) in enumerate(rng))
+
+
+def _gather_worker(rank, world, port, n, k, q):
+    from fastdec_b200.multigpu import block_ranges
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(11)
+        full = rng.integers(0, 2 ** 62, size=(n, k), dtype=np.int64)   # every rank draws the same lists
+        ranges = block_ranges(n, world)
+        a, b = ranges[rank]
+        got = gather_to_root(torch.from_numpy(full[a:b].copy()), n, rank, world, ranges)
+        if rank == 0:
+            assert np.array_equal(got.numpy(), full)
+        else:
+            assert got is None
+        q.put((rank, "ok"))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("n,world", [(1000, 3), (129, 2), (300, 3), (100, 3)])
+def test_gather_of_row_block_ranges(n, world):
+    """The tcgen05 path of the sharded fit: each rank's own row-block range is final and rank 0
+    collects the ranges (uneven widths, a rank with a short or empty range)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, n, 5, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert results == {r: "ok" for r in range(world)}
