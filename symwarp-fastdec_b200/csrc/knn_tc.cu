@@ -26,14 +26,16 @@
 // each delta in the range (T/2 once when T is even), i.e. exactly the candidates the symmetric SIMT
 // round offers every point. A tile is one row block X against two adjacent column blocks
 // (Y, Y + 1) = (X + delta, X + delta + 1); a work item keeps (Y, Y + 1) resident in shared memory
-// and streams the row blocks X = Y - delta, so per 32768 pairs only one 28 KB row block moves.
+// and streams the row blocks X = Y - delta, so per 32768 pairs only one row block (28 KB at
+// d = 50) moves. A shard of the row blocks walks only the column blocks its rows reach.
 //
 // Kernel shape (persistent, one CTA per SM, 16 warps):
 //   warp 0       producer: cp.async.bulk copies of the resident column pair (pre-swizzled 4 KB K
-//                panels in global memory, the SWIZZLE_32B K-major layout) and of up to four row
-//                block stages
+//                panels in global memory, the SWIZZLE_32B K-major layout) and of the row stages:
+//                up to four whole row blocks, or for large K (d > 74) groups of K panels of a
+//                block, several stages per tile (pick_plan)
 //   warp 1       TMEM owner and MMA issuer (one thread): K/8 tcgen05.mma kind::tf32 per tile into
-//                one of two 256-column TMEM accumulators; tcgen05.commit frees the row stage and
+//                one of two 256-column TMEM accumulators; tcgen05.commit frees each row stage and
 //                publishes the accumulator
 //   warps 2..9   filter: tcgen05.ld 32 columns at a time (two loads in flight), sign-bit test; a
 //                row with survivors parks its 32 accumulator words in shared memory and queues
