@@ -138,3 +138,34 @@ def test_gather_of_row_block_ranges(n, world):
     for p in procs:
         p.join(timeout=60)
     assert results == {r: "ok" for r in range(world)}
+
+
+def _dead_peer_worker(rank, world, port, q):
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    if rank == 1:
+        q.put((rank, "left"))
+        q.close()
+        q.join_thread()
+        os._exit(0)   # the peer leaves between steps, before the gather
+    try:
+        gather_to_root(torch.zeros((5, 3), dtype=torch.int64), 10, rank, world)
+        q.put((rank, "no error"))
+    except Exception as e:  # the collective must fail, not wait forever
+        q.put((rank, "error:" + type(e).__name__))
+
+
+def test_gather_with_a_dead_peer_fails_instead_of_hanging():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dead_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert results[1] == "left"
+    assert results[0].startswith("error:")
