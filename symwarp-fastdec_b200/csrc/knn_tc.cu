@@ -50,6 +50,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 namespace fdb {
@@ -94,6 +95,7 @@ struct Args {
     int* ovf;                       // set to tag when a point's candidate count passes cap
     int* err;                       // bounded-wait failure code
     int tag;                        // the round's tag (its index in the host's batch + 1)
+    int withhold_first_row_copy;    // failure injection: the first row stage is never filled
     unsigned long long* counters;   // optional trace counters
 };
 
@@ -498,8 +500,11 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                             const int s = g % S;
                             if (!mbar_wait(&r_empty[s], ((g / S) & 1) ^ 1, abort_flag, a.err, 2)) { ok = false; break; }
                             const uint32_t bytes = (uint32_t)min(a.gp, panels - q * a.gp) * (kRows * 32);
-                            mbar_expect_tx(&r_full[s], bytes);
-                            bulk_load(sm + P.rows + s * P.rstage, rsrc + (size_t)q * a.gp * (kRows * 32), bytes, &r_full[s]);
+                            if (g > 0 || !a.withhold_first_row_copy) {
+                                mbar_expect_tx(&r_full[s], bytes);
+                                bulk_load(sm + P.rows + s * P.rstage, rsrc + (size_t)q * a.gp * (kRows * 32), bytes,
+                                          &r_full[s]);
+                            }
                             ++g;
                         }
                         tw[1] += clock64() - c0;
@@ -508,8 +513,10 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                         const int s = g % S;
                         if (!mbar_wait(&r_empty[s], ((g / S) & 1) ^ 1, abort_flag, a.err, 2)) { ok = false; break; }
                         tw[1] += clock64() - c0;
-                        mbar_expect_tx(&r_full[s], blk_bytes);
-                        bulk_load(sm + P.rows + s * P.rstage, rsrc, blk_bytes, &r_full[s]);
+                        if (g > 0 || !a.withhold_first_row_copy) {
+                            mbar_expect_tx(&r_full[s], blk_bytes);
+                            bulk_load(sm + P.rows + s * P.rstage, rsrc, blk_bytes, &r_full[s]);
+                        }
                         ++g;
                     }
                 }
@@ -972,6 +979,11 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.ovf = r.ovf;
     a.err = r.ovf + 1;
     a.tag = r.tag;
+    // failure injection for the tests: FDB200_FAULT_INJECT=withhold_row_copy leaves every CTA's first
+    // row stage unfilled, so the MMA issuer's bounded wait runs out and the launch ends with an error
+    // code (no fault: every wait of the kernel is bounded and the abort path frees TMEM)
+    const char* inject = getenv("FDB200_FAULT_INJECT");
+    a.withhold_first_row_copy = (inject && std::strcmp(inject, "withhold_row_copy") == 0) ? 1 : 0;
     a.counters = r.counters;
     if (r.diag) {
         a.items = r.nb;
