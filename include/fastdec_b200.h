@@ -35,6 +35,15 @@ enum {
     FDB200_EINTERNAL = -6    /* an internal consistency check failed */
 };
 
+/*
+ * Environment variables the library reads:
+ *   FDB200_TRACE=1                            per-round tile statistics on stderr (diagnostics).
+ *   FDB200_FAULT_INJECT=withhold_row_copy     TEST-ONLY failure injection. Read once per process: the
+ *       first tcgen05 tile launch of the process withholds one shared-memory copy in every CTA, its
+ *       bounded waits run out after about a second, and that call returns FDB200_EINTERNAL; every
+ *       later call runs normally. Never set it in production.
+ */
+
 enum { FDB200_FP32 = 0, FDB200_TF32 = 1 };              /* distance precision */
 enum { FDB200_LAPLACIAN = 0, FDB200_GAUSSIAN = 1 };    /* density kernel (USE_GAUSSIAN_KERNEL) */
 enum { FDB200_ENGINE_AUTO = 0, FDB200_ENGINE_SIMT = 1, FDB200_ENGINE_TCGEN05 = 2 };
@@ -200,9 +209,11 @@ int fdb200_read_csv(const char* path, int n, int d, float* out_dim_major, int th
  * Asynchronous on opts->stream (NULL = the legacy default stream); results are ready when the
  * stream reaches them. The array is shared by all calls on a device, so calls whose executions
  * overlap (two streams, or two host threads with no ordering between them) race and corrupt each
- * other's mean: order them on one stream or with events. The first call on each device looks up
- * the array's address (cudaGetSymbolAddress, which may load the module); make that first call
- * before any stream capture begins.
+ * other's mean: order them on one stream or with events. The first call on each device does a
+ * one-time set-up: it looks up the array's address (cudaGetSymbolAddress) and loads the kernels
+ * this entry point launches (CUDA otherwise loads each kernel lazily, obtaining device memory for
+ * its code, at its first launch); make that first call before any stream capture begins. Later
+ * calls on that device obtain no memory at all.
  */
 #define FDB200_NOALLOC_MAX_POINTS 4194304
 int fdb200_density_noalloc(const float* knn_dist_dev, int n, int k, const FdB200Opts* opts,

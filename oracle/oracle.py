@@ -22,12 +22,23 @@ _lib = None
 _ref = {}
 
 
+def reference_tree():
+    """The reference checkout: $FASTDEC_REF, else a `reference/` directory beside this repository;
+    None when neither holds the reference sources (as on a GPU box, which only uses the prebuilt
+    oracle/_ref files)."""
+    for cand in (os.environ.get("FASTDEC_REF"), str(HERE.parent.parent / "reference")):
+        if cand and (Path(cand) / "fastdecbase.cpp").exists():
+            return Path(cand)
+    return None
+
+
 def build():
     """Compile the oracle library (and oracle/_ref when the reference tree is present)."""
     import subprocess
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
-    if Path("/root/reference/fastdecbase.cpp").exists():
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref"], check=True)
+    ref = reference_tree()
+    if ref is not None:
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={ref}"], check=True)
 
 
 def lib():

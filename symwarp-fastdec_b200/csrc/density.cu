@@ -380,6 +380,20 @@ void density_from_mean(const float* dist, int n, int k, int gaussian, const doub
     FDB_LAUNCHED();
 }
 
+// Loads the kernels of exact_mean_in and density_from_mean on the current device now. With CUDA's
+// lazy loading a kernel's code is loaded (and device memory obtained for it) at its first launch;
+// the allocation-free entry point calls this once per device so that no later call loads anything.
+void preload_mean_density_kernels()
+{
+    cudaFuncAttributes fa;
+    FDB_CUDA(cudaFuncGetAttributes(&fa, chunk_sums_kernel));
+    FDB_CUDA(cudaFuncGetAttributes(&fa, prefix_kernel));
+    FDB_CUDA(cudaFuncGetAttributes(&fa, chunk_maps_kernel));
+    FDB_CUDA(cudaFuncGetAttributes(&fa, compose_level_kernel));
+    FDB_CUDA(cudaFuncGetAttributes(&fa, resolve_mean_kernel));
+    FDB_CUDA(cudaFuncGetAttributes(&fa, density_kernel));
+}
+
 // ------------------------------------------------------------------ DC detection
 namespace {
 

@@ -146,6 +146,9 @@ void exact_mean_in(void* scratch, size_t scratch_bytes, const float* dist_rm, in
                    cudaStream_t s);
 void density_from_mean(const float* dist_rm, int n, int k, int gaussian, const double* mean_dev,
                        float* den, cudaStream_t s);
+// loads the kernels of the two calls above on the current device (CUDA loads kernels lazily, at their
+// first launch, otherwise)
+void preload_mean_density_kernels();
 // parent + ordered core list; returns the core count (synchronises on s)
 int dc_detection(Workspace& ws, const int* idx_rm, const float* den, int n, int k, int* parent,
                  int* cores, cudaStream_t s);

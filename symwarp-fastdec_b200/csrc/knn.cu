@@ -517,7 +517,8 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     float* U = ws.fthr.as<float>(rows);
     uint64_t* cand = ws.cand.as<uint64_t>((size_t)n * cap);
     int* cnt = ws.cnt.as<int>(n);
-    int* ovf = ws.flags.as<int>(16);   // [0] overflow, [1] tcgen05 error, [2..3] admitted, [8..13] trace counters
+    int* ovf = ws.flags.as<int>(16);   // [0] overflow, [1] tcgen05 error, [2..3] admitted, [4] tcgen05 drain
+                                       // timeout, [8..13] trace counters
     unsigned long long* admitted = reinterpret_cast<unsigned long long*>(ovf + 2);
     compute_norms(x, cfg.ldx, n, d, norms, s);
     init_point_state_kernel<<<(rows + 255) / 256, 256, 0, s>>>(n, rows, norms, thr, U);
@@ -635,12 +636,12 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
         if (plan.empty()) break;
 
         // settle the batch: flags and the admitted counter in one copy
-        FDB_CUDA(cudaMemcpyAsync(ws.pinned, ovf, 4 * sizeof(int), cudaMemcpyDeviceToHost, s));
+        FDB_CUDA(cudaMemcpyAsync(ws.pinned, ovf, 8 * sizeof(int), cudaMemcpyDeviceToHost, s));
         unsigned long long cn[16] = {0};
         if (trace) FDB_CUDA(cudaMemcpyAsync(cn, counters, sizeof(cn), cudaMemcpyDeviceToHost, s));
         if (trace) FDB_CUDA(cudaMemsetAsync(counters, 0, sizeof(cn), s));
         FDB_CUDA(cudaStreamSynchronize(s));
-        const int tag = ws.pinned[0], err = ws.pinned[1];
+        const int tag = ws.pinned[0], err = ws.pinned[1], drain_err = ws.pinned[4];
         std::memcpy(&adm, ws.pinned + 2, sizeof(adm));
         const int ran = tag > 0 ? tag : (int)plan.size();   // rounds after an overflowed one did nothing
         for (int i = 1; i <= (int)plan.size(); ++i) {
@@ -649,8 +650,12 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
             res.tile_ms += ms;
         }
         res.rounds += ran;
-        if (err) throw Error(FDB200_EINTERNAL, "tcgen05 tile kernel stopped on a bounded wait (code " +
-                                                   std::to_string(err) + ")");
+        if (err)
+            throw Error(FDB200_EINTERNAL,
+                        "tcgen05 tile kernel stopped on a bounded wait (code " + std::to_string(err) + ")" +
+                            (drain_err ? std::string("; its drain of the ") + (drain_err == 1 ? "copies" : "MMAs") +
+                                             " in flight also ran out, so the device may be unsafe to use"
+                                       : std::string()));
         if (trace) {
             const Planned& pl = plan.back();
             float ms = 0.0f, merge_ms = 0.0f;

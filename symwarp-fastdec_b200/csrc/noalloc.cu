@@ -21,13 +21,16 @@ constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
 void* g_scratch_addr[kMaxDevices] = {};
 
-// the array's address on `device`, looked up on the first call for that device (device current)
+// The array's address on `device`, looked up on the first call for that device (device current).
+// The same one-time set-up also loads every kernel this entry point launches: CUDA loads kernels
+// lazily, at their first launch, and a load obtains device memory for the code.
 void* scratch_on(int device)
 {
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     if (!g_scratch_addr[device]) {
         void* p = nullptr;
         FDB_CUDA(cudaGetSymbolAddress(&p, g_mean_scratch));
+        preload_mean_density_kernels();
         g_scratch_addr[device] = p;
     }
     return g_scratch_addr[device];

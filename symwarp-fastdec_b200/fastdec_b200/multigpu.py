@@ -59,16 +59,20 @@ def gather_to_root(merged: torch.Tensor, n: int, rank: int, world: int, ranges=N
     """merged: (n_own, k) final lists of this rank's points (its range in `ranges`, the owner ranges
     by default). Rank 0 receives the full (n, k).
 
-    A collective (all-gather of equal, padded blocks) rather than point-to-point sends: collectives on
-    one communicator run in the same order on every rank, so a rank that has already moved on to
-    the next step's kernels cannot hold back the transfer that rank 0 is waiting for."""
+    A collective (a gather of equal, padded blocks to rank 0) rather than point-to-point sends:
+    collectives on one communicator run in the same order on every rank, so a rank that has already
+    moved on to the next step's kernels cannot hold back the transfer that rank 0 is waiting for.
+    Only rank 0 receives (and allocates room for) the other ranks' blocks."""
     k = merged.shape[1]
     rng = ranges if ranges is not None else owner_ranges(n, world)
     width = max(b - a for a, b in rng)
-    pad = torch.empty((width, k), dtype=merged.dtype, device=merged.device)
-    pad[:merged.shape[0]].copy_(merged)
-    parts = [torch.empty_like(pad) for _ in range(world)]
-    dist.all_gather(parts, pad)
+    if merged.shape[0] == width and merged.is_contiguous():
+        pad = merged
+    else:
+        pad = torch.empty((width, k), dtype=merged.dtype, device=merged.device)
+        pad[:merged.shape[0]].copy_(merged)
+    parts = [torch.empty_like(pad) for _ in range(world)] if rank == 0 else None
+    dist.gather(pad, gather_list=parts, dst=0)
     if rank != 0:
         return None
     return torch.cat([parts[s][:b - a] for s, (a, b) in enumerate(rng)], dim=0)

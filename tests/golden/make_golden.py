@@ -10,6 +10,7 @@ Writes, next to this script:
                         * two-blob Fit (points, k, c)              symwarp_unit_test.cu:90-144
 The arrays are extracted from the reference files as text, so a change upstream shows up here.
 Usage: python tests/golden/make_golden.py [/path/to/reference]
+(default: $FASTDEC_REF, else a `reference/` directory beside this repository)
 """
 import ctypes
 import json
@@ -38,7 +39,9 @@ def array_literal(src, name, start=0):
 
 
 def main():
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    import os
+    default = os.environ.get("FASTDEC_REF") or str(HERE.parent.parent.parent / "reference")
+    ref = Path(sys.argv[1] if len(sys.argv) > 1 else default)
     libc = ctypes.CDLL(None)
     libc.strtof.restype = ctypes.c_float
     libc.strtof.argtypes = [ctypes.c_char_p, ctypes.c_void_p]
