@@ -170,11 +170,12 @@ int fdb200_lists_to_knn(const uint64_t* lists_dev, int n, int k, const FdB200Opt
                         float* dist_dev, int* idx_dev);
 
 /*
- * Fit from a finished kNN graph already on the device (rank-major dist / idx, k ranks): the
- * stages after build_knn_graph (fastdecbase.cpp:173-227). data is the dim-major dataset
- * (device pointer when opts->inputs_on_device).
+ * Fit from a finished kNN graph (rank-major dist / idx, rank stride n; the first k ranks are used,
+ * so a graph of more ranks serves any smaller k): the stages after build_knn_graph
+ * (fastdecbase.cpp:173-227). data, knn_dist and knn_idx are device pointers when
+ * opts->inputs_on_device, host pointers otherwise.
  */
-int fdb200_fit_from_knn(const float* data, const float* knn_dist_dev, const int* knn_idx_dev,
+int fdb200_fit_from_knn(const float* data, const float* knn_dist, const int* knn_idx,
                         int n, int d, int k, int c, const FdB200Opts* opts, int* centers_out,
                         int* labels_out, float* densities_out, FdB200Stats* stats);
 
@@ -191,6 +192,32 @@ int fdb200_release(const FdB200Opts* opts);
  */
 int fdb200_csv_shape(const char* path, int* n_out, int* d_out);
 int fdb200_read_csv(const char* path, int n, int d, float* out_dim_major, int threads);
+
+/*
+ * The dataset as a binary file (.fbin): int32 n, int32 d, then n * d float32, row-major (one point per
+ * row), little endian. No counterpart in the reference, which reads CSV text only (helper.cpp:9-63):
+ * the same dim-major output as fdb200_read_csv (out_dim_major[t * n + i]) without a text parse.
+ * fdb200_write_fbin writes a dim-major array in that format (e.g. to convert a CSV once).
+ * Host-only; a size that disagrees with the header is FDB200_EINVAL.
+ */
+int fdb200_fbin_shape(const char* path, int* n_out, int* d_out);
+int fdb200_read_fbin(const char* path, int n, int d, float* out_dim_major, int threads);
+int fdb200_write_fbin(const char* path, const float* data_dim_major, int n, int d);
+
+/*
+ * kNN-graph persistence. No counterpart in the reference, which recomputes the graph on every Fit
+ * (build_knn_graph, fastdecbase.cpp:231-255). fdb200_knn_graph_save writes the rank-major graph that
+ * fdb200_knn returns (host pointers; k ranks of n points) with a 32-byte header (magic "FDBKNNG1",
+ * version, n, k, the caller's flags word, a hash of the payload); fdb200_knn_graph_shape reads n, k and
+ * flags back; fdb200_knn_graph_load fills caller buffers of k * n entries, checks the hash and the
+ * index range, and returns FDB200_EINVAL on a mismatch or a damaged file. A graph of k ranks serves
+ * fdb200_fit_from_knn for any k' <= k, so sweeps over k and the cluster count need one kNN.
+ * Host-only.
+ */
+int fdb200_knn_graph_save(const char* path, const float* knn_dist, const int* knn_idx, int n, int k,
+                          int flags);
+int fdb200_knn_graph_shape(const char* path, int* n_out, int* k_out, int* flags_out);
+int fdb200_knn_graph_load(const char* path, int n, int k, float* knn_dist, int* knn_idx);
 
 /*
  * fdb200_density without any allocation. No counterpart in the reference (every reference call,

@@ -192,17 +192,20 @@ def ref_available(gaussian=False):
     return (HERE / "_ref" / name).exists()
 
 
-def ref_fit(x_dm, k, c, gaussian=False):
-    """FastDECBase::Fit from the reference sources (CPU kNN and DC reduction stand-ins)."""
+def _ref_lib(gaussian):
     name = "libfastdec_ref_gauss.so" if gaussian else "libfastdec_ref.so"
     if name not in _ref:
         L = ctypes.CDLL(str(HERE / "_ref" / name))
         ip = ctypes.POINTER(ctypes.c_int)
-        L.ref_fit.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                              _i32p, _i32p, _f32p, _i32p, _i32p, ip, ip, ctypes.c_char_p, ctypes.c_int]
+        tail = [_i32p, _i32p, _f32p, _i32p, _i32p, ip, ip, ctypes.c_char_p, ctypes.c_int]
+        L.ref_fit.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int] + tail
+        L.ref_fit_from_knn.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                       _f32p, _i32p] + tail
         _ref[name] = L
-    L = _ref[name]
-    x = _dm(x_dm)
+    return _ref[name]
+
+
+def _ref_call(fn, x, c, *lead):
     d, n = x.shape
     centers = np.full(c, -1, np.int32)
     labels = np.empty(n, np.int32)
@@ -211,9 +214,29 @@ def ref_fit(x_dm, k, c, gaussian=False):
     cores = np.empty(n, np.int32)
     nc, fk = ctypes.c_int(0), ctypes.c_int(0)
     err = ctypes.create_string_buffer(256)
-    rc = L.ref_fit(x, n, d, k, c, centers, labels, den, parents, cores, ctypes.byref(nc),
-                   ctypes.byref(fk), err, 256)
+    rc = fn(*lead, centers, labels, den, parents, cores, ctypes.byref(nc), ctypes.byref(fk), err, 256)
     if rc != 0:
         raise RuntimeError(err.value.decode() or "ref_fit failed")
     return dict(centers=centers, labels=labels, densities=den, parents=parents,
                 cores=cores[:nc.value].copy(), num_cores=nc.value, final_k=fk.value)
+
+
+def ref_fit(x_dm, k, c, gaussian=False):
+    """FastDECBase::Fit from the reference sources (CPU kNN and DC reduction stand-ins)."""
+    x = _dm(x_dm)
+    d, n = x.shape
+    return _ref_call(_ref_lib(gaussian).ref_fit, x, c, x, n, d, k, c)
+
+
+def ref_fit_from_knn(x_dm, knn_dist_rm, knn_idx_rm, c, gaussian=False):
+    """FastDECBase::Fit from the reference sources on a given kNN graph (rank-major (k, n) distances
+    and indices, e.g. the GPU engine's): the reference's own density, DC detection with k-halving,
+    final clustering, and the oracle's DC reduction. `parents` is the reference's m_cdh_ids after the
+    fit (detection parents, with the cores' DC-reduction parents written in)."""
+    x = _dm(x_dm)
+    d, n = x.shape
+    dist = np.ascontiguousarray(knn_dist_rm, dtype=np.float32)
+    idx = np.ascontiguousarray(knn_idx_rm, dtype=np.int32)
+    k = dist.shape[0]
+    assert dist.shape == (k, n) and idx.shape == (k, n)
+    return _ref_call(_ref_lib(gaussian).ref_fit_from_knn, x, c, x, n, d, k, c, dist, idx)

@@ -61,10 +61,16 @@ bool warp_parallel_dc_reduction_cuda(Dataset& ds, const float* ds_den_host, cons
 
 namespace {
 
+// compute_knn is the oracle's exact CPU kNN, or -- when given_dist / given_idx are set -- a copy of
+// lists the caller already has (rank-major, k ranks, the layout compute_knn returns), so the
+// reference's own stages can be run on another engine's kNN graph
 class CpuKnnFastDEC : public FastDECBase
 {
 public:
-    CpuKnnFastDEC(int k, int c) : FastDECBase(k, c, "oracle_ref_cpu") {}
+    CpuKnnFastDEC(int k, int c, const float* given_dist = nullptr, const int* given_idx = nullptr)
+        : FastDECBase(k, c, "oracle_ref_cpu"), m_given_dist(given_dist), m_given_idx(given_idx)
+    {
+    }
     const real_1d_array& densities() const { return m_densities; }
     const integer_1d_array& parents() const { return m_cdh_ids; }
     int final_k() const { return m_num_k_points; }
@@ -72,9 +78,22 @@ public:
 protected:
     bool compute_knn(Dataset& ds, int k, float* out_dists, int* out_idx) override
     {
+        if (m_given_dist && m_given_idx) {
+            const size_t count = (size_t)ds.num_points() * k;
+            std::memcpy(out_dists, m_given_dist, count * sizeof(float));
+            std::memcpy(out_idx, m_given_idx, count * sizeof(int));
+            return true;
+        }
         return or_knn(ds.host_data(), ds.num_points(), ds.dim(), k, shim_threads(), out_dists, out_idx) == 0;
     }
+
+private:
+    const float* m_given_dist;
+    const int* m_given_idx;
 };
+
+int run_fit(CpuKnnFastDEC& model, const float* x_dm, int n, int d, int c, int* centers, int* labels,
+            float* densities, int* parents, int* cores, int* num_cores, int* final_k, char* err, int err_len);
 
 }  // namespace
 
@@ -84,8 +103,28 @@ extern "C" int ref_fit(const float* x_dm, int n, int d, int k, int c, int* cente
                        float* densities, int* parents, int* cores, int* num_cores, int* final_k,
                        char* err, int err_len)
 {
+    CpuKnnFastDEC model(k, c);
+    return run_fit(model, x_dm, n, d, c, centers, labels, densities, parents, cores, num_cores, final_k, err,
+                   err_len);
+}
+
+// The same Fit on a kNN graph the caller supplies (rank-major knn_dist / knn_idx, k ranks of n
+// points): everything after build_knn_graph is the reference's own code.
+extern "C" int ref_fit_from_knn(const float* x_dm, int n, int d, int k, int c, const float* knn_dist,
+                                const int* knn_idx, int* centers, int* labels, float* densities, int* parents,
+                                int* cores, int* num_cores, int* final_k, char* err, int err_len)
+{
+    CpuKnnFastDEC model(k, c, knn_dist, knn_idx);
+    return run_fit(model, x_dm, n, d, c, centers, labels, densities, parents, cores, num_cores, final_k, err,
+                   err_len);
+}
+
+namespace {
+
+int run_fit(CpuKnnFastDEC& model, const float* x_dm, int n, int d, int c, int* centers, int* labels,
+            float* densities, int* parents, int* cores, int* num_cores, int* final_k, char* err, int err_len)
+{
     try {
-        CpuKnnFastDEC model(k, c);
         model.Fit(x_dm, n, d);
         const integer_1d_array& ctr = model.get_center_indices();
         const integer_1d_array& lab = model.get_labels();
@@ -106,3 +145,5 @@ extern "C" int ref_fit(const float* x_dm, int n, int d, int k, int c, int* cente
         return -2;
     }
 }
+
+}  // namespace

@@ -21,6 +21,11 @@ public:
     // points" is reported exactly as the reference throws it (fastdecbase.cpp:188-191).
     void Fit(const float* data, int num_points, int num_dim);
 
+    // The same fit from a finished kNN graph (host, rank-major, rank stride num_points; its first
+    // k ranks are used), e.g. one loaded with fdb200_knn_graph_load: the stages after
+    // build_knn_graph (fastdecbase.cpp:173-227) without recomputing the kNN.
+    void FitFromKnn(const float* data, int num_points, int num_dim, const float* knn_dist, const int* knn_idx);
+
     const std::vector<int>& get_center_indices() const { return m_centers; }
     const std::vector<int>& get_labels() const { return m_labels; }
     const std::vector<float>& get_densities() const { return m_densities; }

@@ -216,20 +216,21 @@ int fdb200_fit(const float* data, int n, int d, int k, int c, const FdB200Opts* 
     return rc;
 }
 
-int fdb200_fit_from_knn(const float* data, const float* knn_dist_dev, const int* knn_idx_dev, int n, int d,
-                        int k, int c, const FdB200Opts* opts, int* centers_out, int* labels_out,
-                        float* densities_out, FdB200Stats* stats)
+int fdb200_fit_from_knn(const float* data, const float* knn_dist, const int* knn_idx, int n, int d, int k, int c,
+                        const FdB200Opts* opts, int* centers_out, int* labels_out, float* densities_out,
+                        FdB200Stats* stats)
 {
     if (stats) std::memset(stats, 0, sizeof(*stats));
     const int rc = guarded(opts, nullptr, nullptr, [&](Workspace& ws, const FdB200Opts& o, cudaStream_t s) {
-        FDB_REQUIRE(data && knn_dist_dev && knn_idx_dev && centers_out && labels_out,
-                    "fdb200_fit_from_knn: null pointer");
+        FDB_REQUIRE(data && knn_dist && knn_idx && centers_out && labels_out, "fdb200_fit_from_knn: null pointer");
         FDB_REQUIRE(n >= 2 && d >= 1 && c >= 1 && k >= 1 && k < n, "fdb200_fit_from_knn: bad sizes");
         StageTimer tm(s);
         const int a = tm.mark();
         const float* x = upload_f32(ws.data, data, (size_t)n * d, o, s);
-        fit_after_knn(ws, x, n, d, knn_dist_dev, knn_idx_dev, k, c, false, o, s, centers_out, labels_out,
-                      densities_out, stats, tm);
+        // the first k ranks of the graph (rank stride n)
+        const float* dist = upload_f32(ws.dist, knn_dist, (size_t)n * k, o, s);
+        const int* idx = upload_i32(ws.idx, knn_idx, (size_t)n * k, o, s);
+        fit_after_knn(ws, x, n, d, dist, idx, k, c, false, o, s, centers_out, labels_out, densities_out, stats, tm);
         const int f = tm.mark();
         FDB_CUDA(cudaStreamSynchronize(s));
         if (stats) stats->total_ms = tm.ms(a, f);

@@ -63,7 +63,9 @@ class Stats(ctypes.Structure):
 EXPORTS = ["fdb200_opts_init", "fdb200_last_error", "fdb200_abi_version", "fdb200_knn", "fdb200_fit",
            "fdb200_dc_reduction", "fdb200_density", "fdb200_dc_detection", "fdb200_final_cluster",
            "fdb200_knn_partial", "fdb200_merge_lists", "fdb200_lists_to_knn", "fdb200_fit_from_knn",
-           "fdb200_release", "fdb200_density_noalloc", "fdb200_csv_shape", "fdb200_read_csv"]
+           "fdb200_release", "fdb200_density_noalloc", "fdb200_csv_shape", "fdb200_read_csv",
+           "fdb200_fbin_shape", "fdb200_read_fbin", "fdb200_write_fbin", "fdb200_knn_graph_save",
+           "fdb200_knn_graph_shape", "fdb200_knn_graph_load"]
 
 _lib = None
 
@@ -96,6 +98,15 @@ def lib():
         L.fdb200_lists_to_knn.argtypes = [vp, i, i, op, vp, vp]
         L.fdb200_fit_from_knn.argtypes = [vp, vp, vp, i, i, i, i, op, vp, vp, vp, sp]
         L.fdb200_release.argtypes = [op]
+        cp, ipp = ctypes.c_char_p, ctypes.POINTER(ctypes.c_int)
+        L.fdb200_csv_shape.argtypes = [cp, ipp, ipp]
+        L.fdb200_read_csv.argtypes = [cp, i, i, vp, i]
+        L.fdb200_fbin_shape.argtypes = [cp, ipp, ipp]
+        L.fdb200_read_fbin.argtypes = [cp, i, i, vp, i]
+        L.fdb200_write_fbin.argtypes = [cp, vp, i, i]
+        L.fdb200_knn_graph_save.argtypes = [cp, vp, vp, i, i, i]
+        L.fdb200_knn_graph_shape.argtypes = [cp, ipp, ipp, ipp]
+        L.fdb200_knn_graph_load.argtypes = [cp, i, i, vp, vp]
         _lib = L
     return _lib
 
@@ -166,6 +177,59 @@ def read_csv(path, threads=0):
     out = np.empty((d.value, n.value), np.float32)
     _check(lib().fdb200_read_csv(p, n.value, d.value, _ptr(out), int(threads)))
     return out
+
+
+def read_fbin(path, threads=0):
+    """A binary dataset file (int32 n, int32 d, then n x d float32 row-major) as a dim-major (d, n)
+    float32 array (fdb200_fbin_shape / fdb200_read_fbin)."""
+    n, d = ctypes.c_int(0), ctypes.c_int(0)
+    p = str(path).encode()
+    _check(lib().fdb200_fbin_shape(p, ctypes.byref(n), ctypes.byref(d)))
+    out = np.empty((d.value, n.value), np.float32)
+    _check(lib().fdb200_read_fbin(p, n.value, d.value, _ptr(out), int(threads)))
+    return out
+
+
+def write_fbin(path, data_dm):
+    """Writes a dim-major (d, n) float32 array as a binary dataset file (fdb200_write_fbin)."""
+    x = _f32(data_dm)
+    d, n = x.shape
+    _check(lib().fdb200_write_fbin(str(path).encode(), _ptr(x), n, d))
+
+
+def save_knn_graph(path, dist_rm, idx_rm, flags=0):
+    """Saves a rank-major (k, n) kNN graph (fdb200_knn_graph_save)."""
+    dist, idx = _f32(dist_rm), _i32(idx_rm)
+    k, n = dist.shape
+    assert idx.shape == (k, n)
+    _check(lib().fdb200_knn_graph_save(str(path).encode(), _ptr(dist), _ptr(idx), n, k, int(flags)))
+
+
+def load_knn_graph(path):
+    """Loads a saved kNN graph: (dist (k, n), idx (k, n), flags)."""
+    n, k, fl = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    p = str(path).encode()
+    _check(lib().fdb200_knn_graph_shape(p, ctypes.byref(n), ctypes.byref(k), ctypes.byref(fl)))
+    dist = np.empty((k.value, n.value), np.float32)
+    idx = np.empty((k.value, n.value), np.int32)
+    _check(lib().fdb200_knn_graph_load(p, n.value, k.value, _ptr(dist), _ptr(idx)))
+    return dist, idx, fl.value
+
+
+def fit_from_knn(data_dm, dist_rm, idx_rm, k, c, **kw):
+    """The fit's stages after the kNN on a given rank-major graph (host arrays): the first k ranks
+    of dist / idx are used. Returns dict(centers, labels, densities, stats)."""
+    x = _f32(data_dm)
+    d, n = x.shape
+    dist, idx = _f32(dist_rm), _i32(idx_rm)
+    assert dist.shape[1] == n and idx.shape == dist.shape and k <= dist.shape[0]
+    centers = np.full(c, -1, np.int32)
+    labels = np.full(n, -1, np.int32)
+    den = np.zeros(n, np.float32)
+    st = Stats()
+    _check(lib().fdb200_fit_from_knn(_ptr(x), _ptr(dist), _ptr(idx), n, d, k, c, ctypes.byref(make_opts(**kw)),
+                                     _ptr(centers), _ptr(labels), _ptr(den), ctypes.byref(st)))
+    return dict(centers=centers, labels=labels, densities=den, stats=st.as_dict())
 
 
 def fit(data_dm, k, c, **kw):

@@ -1,6 +1,7 @@
 """The sharded fit on two GPUs (one process per GPU, NCCL): the kNN triangle split by row blocks, the
-partial lists exchanged to their owners with an all-to-all, merged, gathered on rank 0, and the fit
-finished there must give exactly the single-GPU centers and labels. Skipped on a one-GPU machine."""
+partial lists exchanged to their owners with an all-to-all (SIMT engine) and merged, gathered on rank
+0, and the fit finished there must give exactly the single-GPU centers and labels. Skipped on a
+one-GPU machine."""
 import os
 import socket
 
@@ -14,7 +15,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, n, q):
+def _rank(rank, world, port, n, q, engine):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -32,14 +33,14 @@ def _rank(rank, world, port, n, q):
         xd = torch.from_numpy(x).to(dev)
         k, c = 30, 10
         sp = torch.cuda.current_stream(dev).cuda_stream
-        runner = ShardedFit(n, 50, k, c, rank, world, dev, sp)
+        runner = ShardedFit(n, 50, k, c, rank, world, dev, sp, engine=engine)
         centers = torch.empty(c, dtype=torch.int32, device=dev)
         labels = torch.empty(n, dtype=torch.int32, device=dev)
         for _ in range(2):   # twice: buffers and lists are reused across steps
             runner.step(xd, centers, labels)
         torch.cuda.synchronize(dev)
         if rank == 0:
-            ref = fdb.fit(x, k, c)
+            ref = fdb.fit(x, k, c, engine=engine)
             same = (centers.cpu().numpy().tolist() == ref["centers"].tolist()
                     and np.array_equal(labels.cpu().numpy(), ref["labels"]))
             q.put((rank, "ok" if same else "mismatch"))
@@ -53,7 +54,10 @@ def _rank(rank, world, port, n, q):
 
 
 @pytest.mark.gpu
-def test_sharded_fit_on_two_gpus_matches_one_gpu():
+@pytest.mark.parametrize("engine", ["auto", "simt"])
+def test_sharded_fit_on_two_gpus_matches_one_gpu(engine):
+    """engine auto: tcgen05 shards, each rank's rows final, gather only. engine simt: symmetric tiles,
+    partial lists for every point, the NCCL all-to-all to the owners and fdb200_merge_lists."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -61,7 +65,7 @@ def test_sharded_fit_on_two_gpus_matches_one_gpu():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, 150_000, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, 150_000 if engine == "auto" else 40_000, q, engine)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in range(2))

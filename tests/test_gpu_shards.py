@@ -2,13 +2,13 @@
 shard = (rank, world)), so the sharded kernel path is covered on a one-GPU box. With the tcgen05 engine
 a shard tests its own row blocks against every column block, so the lists of its own points are final
 and the shards' ranges put together equal the unsharded lists. With the SIMT engine (symmetric tiles)
-every shard holds partial lists for all points, and their per-point merge (the k smallest keys) equals
-the unsharded lists."""
+every shard holds partial lists for all points, and their per-point merge by the library
+(fdb200_merge_lists, the k smallest keys) equals the unsharded lists."""
 import numpy as np
 import pytest
 
 from fastdec_b200.datasets import embedding_cloud, scale_out
-from fastdec_b200.multigpu import block_ranges
+from fastdec_b200.multigpu import block_ranges, owner_ranges
 
 pytestmark = pytest.mark.gpu
 
@@ -35,7 +35,16 @@ def test_shards_on_one_gpu_equal_the_unsharded_lists(fdb, world, engine):
     if engine == "tcgen05":
         got = np.concatenate([p[a:b] for (p, _), (a, b) in zip(parts, block_ranges(n, world))])
     else:
-        got = np.sort(np.concatenate([p for p, _ in parts], axis=1), axis=1)[:, :k]
+        # the owners' merge of the exchanged partial lists, by the library (fdb200_merge_lists), for
+        # each owner range as ShardedFit runs it after the all-to-all
+        got = np.empty_like(full)
+        for a, b in owner_ranges(n, world):
+            own = torch.from_numpy(parts[0][0][a:b].view(np.int64).copy()).cuda()
+            srcs = torch.from_numpy(np.stack([p[a:b].view(np.int64) for p, _ in parts[1:]])).cuda()
+            fdb.merge_lists_device(own, srcs, world - 1, b - a, k)
+            got[a:b] = own.cpu().numpy().view(np.uint64)
+        # and the same selection restated on the host
+        assert np.array_equal(np.sort(np.concatenate([p for p, _ in parts], axis=1), axis=1)[:, :k], full)
     assert np.array_equal(got, full)
 
 
