@@ -673,9 +673,10 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
                 const double tiles = cn[3] > 0 ? (double)cn[3] : 1.0;
                 const double per_f = tiles * 8.0;   // filter warp-tiles (each tile has one refine warp)
                 fprintf(stderr, "[fdb200]   cycles/tile: producer wait cols %.0f rows %.0f | filter wait %.0f work %.0f |"
-                                " refine wait %.0f work %.0f | entries/tile %.1f inline %llu | mma loop %.0f\n",
+                                " refine wait %.0f work %.0f | entries/tile %.1f inline %llu | mma loop %.0f"
+                                " (waits: row stage %.0f, accumulator %.0f)\n",
                         cn[4] / tiles, cn[5] / tiles, cn[9] / per_f, cn[10] / per_f, cn[11] / tiles, cn[12] / tiles,
-                        cn[0] / tiles, cn[1], cn[15] / tiles);
+                        cn[0] / tiles, cn[1], cn[15] / tiles, cn[6] / tiles, cn[7] / tiles);
             }
         }
         if (tag > 0) {

@@ -132,7 +132,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity)
 
 // trace-mode phase timers: cycles accumulated per role, added to counters[4 + slot] at the end
 enum {
-    kTProdWaitCols = 0, kTProdWaitRows = 1, kTFiltWait = 5, kTFiltWork = 6, kTRefWait = 7, kTRefWork = 8
+    kTProdWaitCols = 0, kTProdWaitRows = 1, kTMmaWaitRows = 2, kTMmaWaitAcc = 3, kTFiltWait = 5, kTFiltWork = 6,
+    kTRefWait = 7, kTRefWork = 8
 };
 
 // bounded wait: false on timeout or when another role aborted the CTA
@@ -555,6 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
             int g = 0, ti = 0, s = 0;
             uint32_t rph = 0;   // parity of the next row-stage fill
             bool ok = true, issued = false;
+            long long mw[2] = {0, 0};   // trace: waits for a row stage, for an accumulator
             const long long t_start = clock64();
             const uint64_t cdesc = sw32_desc(su32(sm + P.cols));
             const uint64_t rdesc0 = sw32_desc(su32(sm + P.rows));
@@ -592,8 +594,14 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                         }
                         if (!ok) break;
                     } else {
+                        const long long w0 = a.counters ? clock64() : 0;
                         if (!mbar_wait_fast(&r_full[s], rph, abort_flag, a.err, 4)) { ok = false; break; }
+                        const long long w1 = a.counters ? clock64() : 0;
                         if (!mbar_wait_fast(&acc_empty[acc], ((g >> 1) & 1) ^ 1, abort_flag, a.err, 5)) { ok = false; break; }
+                        if (a.counters) {
+                            mw[0] += w1 - w0;
+                            mw[1] += clock64() - w1;
+                        }
                         tc_fence_after();
                         const uint64_t ad = rdesc0 + (uint64_t)s * rstride;
                         for (int p = 0; p < panels; ++p)
@@ -627,6 +635,8 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
             if (a.counters) {
                 atomicAdd(&a.counters[3], (unsigned long long)g);
                 atomicAdd(&a.counters[15], (unsigned long long)(clock64() - t_start));
+                atomicAdd(&a.counters[4 + kTMmaWaitRows], (unsigned long long)mw[0]);
+                atomicAdd(&a.counters[4 + kTMmaWaitAcc], (unsigned long long)mw[1]);
             }
         }
         __syncwarp();
