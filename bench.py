@@ -69,6 +69,9 @@ def parse():
     p.add_argument("--engine", default="auto", choices=["auto", "simt", "tcgen05"])
     p.add_argument("--seed", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-reference-gpu", action="store_true",
+                   help="skip timing the reference's own GPU Fit (oracle/_ref binaries) at N=1")
+    p.add_argument("--reference-gpu-runs", type=int, default=2)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=8.0, help="target CPU seconds per reference sample")
     a = p.parse_args()
@@ -226,6 +229,37 @@ def run_reference_sample(x_full, a, target_s, steps=1, warmup=0):
                 seconds_per_fit=mean_s, n_sample=ns)
 
 
+def run_reference_gpu(x_host, a, centers):
+    """The reference's own GPU Fit on the same data and GPU (its symwarp backend built unmodified from its
+    sources into oracle/_ref by `make -C oracle refgpu`), with its host CPU stages on all host cores
+    (FASTDEC_DENSITY_THREADS=0); outside every timed region. A baseline, like cpu_baseline."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import run_reference_gpu as rg
+    out = {}
+    builds = {"fds": "symwarp-fastdec-fds", "tf32_gaussian": "symwarp-fastdec-tf32g"}
+    key = "tf32_gaussian" if (a.precision, a.density) == ("tf32", "gaussian") else "fds"
+    if a.precision == "tf32" and key != "tf32_gaussian":
+        return {"unavailable": "the reference's TF32 build is built with the Gaussian kernel only"}
+    binary = ROOT / "oracle" / "_ref" / builds[key]
+    if not binary.exists():
+        return {"unavailable": f"{binary.name} not built (make -C oracle refgpu)"}
+    try:
+        r = rg.time_reference_gpu(x_host, a.k, a.c, binary, runs=a.reference_gpu_runs)
+    except Exception as e:   # a baseline that fails must not take the bench line with it
+        return {"unavailable": f"reference run failed: {e!r}"[:300]}
+    fit = r["fit_s_per_run"]
+    out = {"build": key, "binary": r["binary"], "rc": r["rc"], "fit_s_per_run": fit,
+           "fit_s_best": min(fit) if fit else None, "stage_s": r["stage_s"],
+           "host_cores": r["host_cores"], "density_threads": "0 (all host cores)",
+           "prep_cpu_s": r["prep_cpu_s"], "centers_equal_ours": r["centers"] == centers,
+           "note": "the reference's own timers (rusage of its host thread, which tracks wall time since the "
+                   "CUDA runtime spin-waits); kNN and DC reduction on this GPU, density / DC detection / final "
+                   "clustering on the host cores"}
+    if r["rc"] != 0:
+        out["stdout_tail"] = r["stdout_tail"]
+    return out
+
+
 # ------------------------------------------------------------------ our engine
 def main():
     a = parse()
@@ -362,6 +396,10 @@ def main():
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         ref = run_reference_sample(x_host, a, a.cpu_seconds)
         cpu = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    ref_gpu = None
+    if rank == 0 and world == 1 and not a.no_reference_gpu:
+        progress("reference GPU fit")
+        ref_gpu = run_reference_gpu(x_host, a, centers.cpu().tolist())
 
     if world > 1:
         dist.barrier()
@@ -399,7 +437,7 @@ def main():
            "num_cores": last.get("num_cores"), "final_k": last.get("final_k"),
            "engine_used": engine_name(stats),
            "centers": centers.cpu().tolist(), "gpu_launches": launches, "clocks": clk.summary(),
-           "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+           "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "reference_gpu": ref_gpu,
            "vs_baseline_note": "value / (8.3353e11 pairs / 16.49 s): the reference's published symwarp FP32 "
                                "Fit on GloVe 50d, RTX A6000 (README.md:149)"}
     print(json.dumps(out), flush=True)

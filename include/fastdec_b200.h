@@ -194,6 +194,14 @@ int fdb200_csv_shape(const char* path, int* n_out, int* d_out);
 int fdb200_read_csv(const char* path, int n, int d, float* out_dim_major, int threads);
 
 /*
+ * Writes a dim-major dataset (data_dim_major[t * n + i]) in the reference CLI's CSV format: one point per
+ * line, comma-separated, each value as the shortest text that reads back (strtof) as the same float, so
+ * the reference's read_data (helper.cpp:30-63) and fdb200_read_csv recover the exact float32 values. No
+ * counterpart in the reference (it only reads). Host-only; threads as in fdb200_read_csv.
+ */
+int fdb200_write_csv(const char* path, const float* data_dim_major, int n, int d, int threads);
+
+/*
  * The dataset as a binary file (.fbin): int32 n, int32 d, then n * d float32, row-major (one point per
  * row), little endian. No counterpart in the reference, which reads CSV text only (helper.cpp:9-63):
  * the same dim-major output as fdb200_read_csv (out_dim_major[t * n + i]) without a text parse.

@@ -10,7 +10,9 @@ It writes the dataset as the reference's CSV input (one point per line, shortest
 text, so the reference parses exactly the float32 values bench.py uses), a 4-line config (CSV path,
 k, clusters, runs; test.cpp:314-335), runs the binary, and prints one JSON line with the wall time
 of the whole process, the reference's own per-run timer lines ("Finished run i of ...", rusage CPU
-seconds of the host thread; the CUDA runtime spin-waits, so they track wall time) and the centers.
+seconds of the host thread; the CUDA runtime spin-waits, so they track wall time), its per-stage
+timers (FASTDEC_STAGE_TIMING builds) and the centers. bench.py imports time_reference_gpu for its
+reference_gpu field.
 """
 from __future__ import annotations
 
@@ -27,11 +29,50 @@ sys.path.insert(0, str(ROOT / "symwarp-fastdec_b200"))
 
 
 def write_csv(x_dm, path):
-    xt = x_dm.T
-    with open(path, "w") as f:
-        for s in range(0, xt.shape[0], 65536):
-            blk = xt[s:s + 65536]
-            f.write("\n".join(",".join(r) for r in blk.astype(str).tolist()) + "\n")
+    """the reference CLI's CSV input, written by the library (shortest round-trip float text, so
+    read_data parses back the exact float32 values)"""
+    import fastdec_b200 as fdb
+    fdb.write_csv(path, x_dm)
+
+
+def time_reference_gpu(x_dm, k, c, binary, runs=2, backend="symwarp", workdir="/tmp/fdb_refgpu",
+                       density_threads=0, timeout=900):
+    """Runs the reference binary on x_dm (dim-major float32) and returns its own timers: Fit seconds
+    per run, the per-stage seconds (kNN on the GPU; density, DC detection and final clustering on the
+    host cores, with FASTDEC_DENSITY_THREADS=density_threads, 0 = all cores), and the centers."""
+    import os
+    wd = Path(workdir)
+    wd.mkdir(parents=True, exist_ok=True)
+    d, n = x_dm.shape
+    csv = wd / f"data_{n}x{d}.csv"
+    t0 = time.time()
+    write_csv(x_dm, csv)
+    t_csv = time.time() - t0
+    cfg = wd / "config.txt"
+    cfg.write_text(f"{csv}\n{k}\n{c}\n{runs}\n")
+    env = dict(os.environ, FASTDEC_DENSITY_THREADS=str(density_threads))
+    t0 = time.time()
+    r = subprocess.run([str(binary), "--backend", backend, str(cfg)], capture_output=True, text=True, env=env,
+                       timeout=timeout)
+    wall = time.time() - t0
+    out = r.stdout
+    fit = [float(m.group(2)) for m in re.finditer(r"Finished run (\d+) of [^:]*: ([0-9.eE+-]+)", out)]
+    stages = {}
+    for m in re.finditer(r"Finished (building kNN graph|density estimation|DC detection|DC reduction|final clustering): "
+                         r"([0-9.eE+-]+)", out):
+        stages.setdefault(m.group(1), []).append(float(m.group(2)))
+    prep = re.search(r"Finished preparation of data including Transpose: ([0-9.eE+-]+)", out)
+    centers = re.findall(r"Cluster centers found: \s*\nlength: \d+\n(\[.*\])", out)
+    try:
+        csv.unlink()
+    except OSError:
+        pass
+    return {"binary": Path(binary).name, "backend": backend, "rc": r.returncode, "n": n, "d": d, "k": k, "c": c,
+            "runs": runs, "process_wall_s": wall, "csv_write_s": t_csv,
+            "prep_cpu_s": float(prep.group(1)) if prep else None, "fit_s_per_run": fit, "stage_s": stages,
+            "density_threads": density_threads, "host_cores": os.cpu_count(),
+            "centers": json.loads(centers[-1]) if centers else None,
+            "stdout_tail": out[-600:] if r.returncode else "", "stderr_tail": r.stderr[-400:]}
 
 
 def main():
@@ -44,37 +85,14 @@ def main():
     p.add_argument("--c", type=int, default=20)
     p.add_argument("--runs", type=int, default=3)
     p.add_argument("--seed", type=int, default=3)
+    p.add_argument("--density-threads", type=int, default=0)
     p.add_argument("--workdir", default="/tmp/fdb_refgpu")
     a = p.parse_args()
     from fastdec_b200.datasets import embedding_cloud
-    wd = Path(a.workdir)
-    wd.mkdir(parents=True, exist_ok=True)
-    csv = wd / f"cloud_{a.n}x{a.d}_s{a.seed}.csv"
-    t0 = time.time()
-    if not csv.exists():
-        write_csv(embedding_cloud(n=a.n, d=a.d, seed=a.seed), csv)
-    t_csv = time.time() - t0
-    cfg = wd / "config.txt"
-    cfg.write_text(f"{csv}\n{a.k}\n{a.c}\n{a.runs}\n")
-    t0 = time.time()
-    r = subprocess.run([a.binary, "--backend", a.backend, str(cfg)], capture_output=True, text=True)
-    wall = time.time() - t0
-    out = r.stdout
-    runs = [float(m.group(2)) for m in re.finditer(r"Finished run (\d+) of [^:]*: ([0-9.eE+-]+)", out)]
-    stages = {}
-    for m in re.finditer(r"Finished (building kNN graph|density estimation|DC detection|DC reduction|final clustering): "
-                         r"([0-9.eE+-]+)", out):
-        stages.setdefault(m.group(1), []).append(float(m.group(2)))
-    prep = re.search(r"Finished preparation of data including Transpose: ([0-9.eE+-]+)", out)
-    centers = re.findall(r"Cluster centers found: \s*\nlength: \d+\n(\[.*\])", out)
-    print(json.dumps({"binary": Path(a.binary).name, "backend": a.backend, "rc": r.returncode, "n": a.n, "d": a.d,
-                      "k": a.k, "c": a.c, "runs": a.runs, "process_wall_s": wall, "csv_write_s": t_csv,
-                      "prep_cpu_s": float(prep.group(1)) if prep else None, "fit_s_per_run": runs,
-                      "stage_s": stages, "centers": json.loads(centers[-1]) if centers else None,
-                      "stderr_tail": r.stderr[-400:]}), flush=True)
-    if r.returncode != 0:
-        print(out[-2000:], file=sys.stderr)
-    return r.returncode
+    res = time_reference_gpu(embedding_cloud(n=a.n, d=a.d, seed=a.seed), a.k, a.c, a.binary, a.runs, a.backend,
+                             a.workdir, a.density_threads)
+    print(json.dumps(res), flush=True)
+    return res["rc"]
 
 
 if __name__ == "__main__":

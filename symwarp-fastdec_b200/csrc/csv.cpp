@@ -200,3 +200,48 @@ extern "C" int fdb200_read_csv(const char* path, int n, int d, float* out_dim_ma
         return FDB200_EINTERNAL;
     }
 }
+
+extern "C" int fdb200_write_csv(const char* path, const float* data_dim_major, int n, int d, int threads)
+{
+    using namespace fdb;
+    try {
+        FDB_REQUIRE(path && data_dim_major && n > 0 && d > 0, "fdb200_write_csv: bad arguments");
+        // each thread formats a contiguous range of rows (shortest text that reads back as the same
+        // float, std::to_chars), then the ranges are written in order
+        const int T = nthreads(threads);
+        std::vector<std::string> part(T);
+        std::vector<std::thread> pool;
+        for (int t = 0; t < T; ++t)
+            pool.emplace_back([&, t] {
+                const long long lo = (long long)n * t / T, hi = (long long)n * (t + 1) / T;
+                std::string& out = part[t];
+                out.reserve((size_t)(hi - lo) * d * 12);
+                char buf[64];
+                for (long long i = lo; i < hi; ++i) {
+                    for (int k = 0; k < d; ++k) {
+                        const auto r = std::to_chars(buf, buf + sizeof(buf), data_dim_major[(size_t)k * n + i]);
+                        out.append(buf, r.ptr);
+                        out.push_back(k + 1 < d ? ',' : '\n');
+                    }
+                }
+            });
+        for (auto& th : pool) th.join();
+        FILE* f = fopen(path, "wb");
+        FDB_REQUIRE(f, std::string("fdb200_write_csv: cannot create ") + path);
+        bool ok = true;
+        for (const std::string& s : part) ok = ok && fwrite(s.data(), 1, s.size(), f) == s.size();
+        ok = (fclose(f) == 0) && ok;
+        FDB_REQUIRE(ok, std::string("fdb200_write_csv: write failed for ") + path);
+        set_last_error("");
+        return FDB200_OK;
+    } catch (const Error& e) {
+        set_last_error(e.what());
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        set_last_error("fdb200_write_csv: host allocation failed");
+        return FDB200_ENOMEM;
+    } catch (const std::exception& e) {
+        set_last_error(e.what());
+        return FDB200_EINTERNAL;
+    }
+}

@@ -64,7 +64,7 @@ EXPORTS = ["fdb200_opts_init", "fdb200_last_error", "fdb200_abi_version", "fdb20
            "fdb200_dc_reduction", "fdb200_density", "fdb200_dc_detection", "fdb200_final_cluster",
            "fdb200_knn_partial", "fdb200_merge_lists", "fdb200_lists_to_knn", "fdb200_fit_from_knn",
            "fdb200_release", "fdb200_density_noalloc", "fdb200_csv_shape", "fdb200_read_csv",
-           "fdb200_fbin_shape", "fdb200_read_fbin", "fdb200_write_fbin", "fdb200_knn_graph_save",
+           "fdb200_write_csv", "fdb200_fbin_shape", "fdb200_read_fbin", "fdb200_write_fbin", "fdb200_knn_graph_save",
            "fdb200_knn_graph_shape", "fdb200_knn_graph_load"]
 
 _lib = None
@@ -101,6 +101,7 @@ def lib():
         cp, ipp = ctypes.c_char_p, ctypes.POINTER(ctypes.c_int)
         L.fdb200_csv_shape.argtypes = [cp, ipp, ipp]
         L.fdb200_read_csv.argtypes = [cp, i, i, vp, i]
+        L.fdb200_write_csv.argtypes = [cp, vp, i, i, i]
         L.fdb200_fbin_shape.argtypes = [cp, ipp, ipp]
         L.fdb200_read_fbin.argtypes = [cp, i, i, vp, i]
         L.fdb200_write_fbin.argtypes = [cp, vp, i, i]
@@ -177,6 +178,14 @@ def read_csv(path, threads=0):
     out = np.empty((d.value, n.value), np.float32)
     _check(lib().fdb200_read_csv(p, n.value, d.value, _ptr(out), int(threads)))
     return out
+
+
+def write_csv(path, data_dm, threads=0):
+    """Writes a dim-major (d, n) float32 array in the reference CLI's CSV format (fdb200_write_csv):
+    one point per line, values as the shortest text that reads back to the same float."""
+    x = _f32(data_dm)
+    d, n = x.shape
+    _check(lib().fdb200_write_csv(str(path).encode(), _ptr(x), n, d, int(threads)))
 
 
 def read_fbin(path, threads=0):

@@ -78,3 +78,23 @@ def test_read_csv_rejects_ragged_rows_and_missing_files(tmp_path):
         fdb.read_csv(p)
     with pytest.raises(fdb.FastDecError, match="cannot read"):
         fdb.read_csv(tmp_path / "missing.csv")
+
+
+def test_write_csv_reads_back_exactly_with_the_reference_parser(tmp_path):
+    """fdb200_write_csv: shortest round-trip text, so both the reference's read_data and the library's
+    reader recover every float32 bit (subnormals, signed zero and extreme exponents included)."""
+    rng = np.random.default_rng(11)
+    n, d = 3001, 9
+    x = (rng.standard_normal((d, n)) * 10.0 ** rng.integers(-30, 30, size=(d, n))).astype(np.float32)
+    x[0, :6] = [0.0, -0.0, 1e-45, -3.4028235e38, 1.1754944e-38, np.float32(0.1)]
+    p = tmp_path / "w.csv"
+    for threads in (1, 5):
+        fdb.write_csv(p, x, threads=threads)
+        got = fdb.read_csv(p)
+        assert np.array_equal(got.view(np.uint32), x.view(np.uint32))
+    if REF_LIB.exists():
+        ref = _ref_read(p, n, d)
+        assert np.array_equal(ref.view(np.uint32), x.T.view(np.uint32))
+    lines = p.read_text().splitlines()
+    # line i is point i (column i of the dim-major array): point 1 starts with -0
+    assert len(lines) == n and lines[1].split(",")[0] == "-0" and lines[0].split(",")[0] == "0"
