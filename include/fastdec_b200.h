@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define FDB200_ABI_VERSION 1
+#define FDB200_ABI_VERSION 2
 
 enum {
     FDB200_OK = 0,
@@ -65,6 +65,8 @@ typedef struct FdB200Opts {
     int cand_capacity;        /* per-point candidate slots per round (0 = automatic) */
     void* stream;             /* cudaStream_t to run on; NULL = the library's own stream (pass
                                  cudaStreamLegacy to run on the legacy default stream) */
+    int shard_block_lo;       /* explicit shard: the 128-point row blocks [shard_block_lo, shard_block_hi) */
+    int shard_block_hi;       /* (-1, -1 = the even split given by shard_rank / shard_count) */
 } FdB200Opts;
 
 typedef struct FdB200Stats {
@@ -178,6 +180,35 @@ int fdb200_lists_to_knn(const uint64_t* lists_dev, int n, int k, const FdB200Opt
 int fdb200_fit_from_knn(const float* data, const float* knn_dist, const int* knn_idx,
                         int n, int d, int k, int c, const FdB200Opts* opts, int* centers_out,
                         int* labels_out, float* densities_out, FdB200Stats* stats);
+
+/*
+ * The fit's stages after the kNN, split so that a multi-GPU caller can shard the DC reduction (the
+ * reference's dc_reduction_cuda, dcreductioncuda.cu:189-545, is a cores x N contraction; here every GPU
+ * reduces its own range of points and the partial results combine). No counterpart in the reference,
+ * which is single-GPU; run on one GPU over [0, n) they give fdb200_fit_from_knn's results.
+ *
+ * fdb200_density_detection: density and DC detection with the k-halving retry while cores < c
+ *   (fastdecbase.cpp:173-199) from a rank-major graph (rank stride n): densities_out n floats,
+ *   parent_out n ints, cores_out (capacity n) the cores in ascending order, *num_cores_out their count,
+ *   *final_k_out the k after halving. FDB200_ECORES when even k = 1 gives fewer than c cores.
+ * fdb200_dc_stage (device pointers): stage 0 writes best_dev[i] = the lexicographic minimum packed key
+ *   ((uint64)float_bits(d2) << 32 | index) over the points of [p_lo, p_hi) strictly denser than core i
+ *   (UINT64_MAX when none); keys of several ranges combine by minimum. Stage 1 reads the combined keys
+ *   and writes rank_dev[i] = the points of [p_lo, p_hi) closer to core i than that parent; ranks of
+ *   several ranges combine by sum (dcreductioncuda.cu:63-170).
+ * fdb200_dc_select (device pointers): from the combined keys and ranks, core_parent_dev (-1 when no
+ *   denser point) and centers_dev (num_centers global indices, -1 padded), as
+ *   warp_parallel_dc_reduction_cuda returns them (dcreductioncuda.cu:113-187, 548-619).
+ */
+int fdb200_density_detection(const float* knn_dist, const int* knn_idx, int n, int k, int c, const FdB200Opts* opts,
+                             float* densities_out, int* parent_out, int* cores_out, int* num_cores_out,
+                             int* final_k_out);
+int fdb200_dc_stage(int stage, const float* data_dev, int n, int d, const float* densities_dev,
+                    const int* cores_dev, int core_nb, int p_lo, int p_hi, const FdB200Opts* opts,
+                    uint64_t* best_dev, int* rank_dev);
+int fdb200_dc_select(const float* densities_dev, const int* cores_dev, int core_nb, const uint64_t* best_dev,
+                     const int* rank_dev, int num_centers, const FdB200Opts* opts, int* core_parent_dev,
+                     int* centers_dev);
 
 /* Frees the library's cached device workspace on opts->device. */
 int fdb200_release(const FdB200Opts* opts);

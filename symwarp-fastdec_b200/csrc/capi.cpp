@@ -49,6 +49,8 @@ KnnConfig knn_config(int n, int d, int k, const FdB200Opts& o)
     c.shard_rank = o.shard_rank;
     c.shard_count = o.shard_count;
     c.cand_capacity = o.cand_capacity;
+    c.block_lo = o.shard_block_lo;
+    c.block_hi = o.shard_block_hi;
     return c;
 }
 
@@ -146,6 +148,8 @@ int fdb200_opts_init(FdB200Opts* opts)
     opts->engine = FDB200_ENGINE_AUTO;
     opts->shard_rank = 0;
     opts->shard_count = 1;
+    opts->shard_block_lo = -1;
+    opts->shard_block_hi = -1;
     return FDB200_OK;
 }
 
@@ -315,6 +319,72 @@ int fdb200_final_cluster(const int* parent, int n, const int* centers, int c, co
         }
         final_cluster(ws, par, n, b.centers, c, b.labels, s);
         download(labels_out, b.labels, sizeof(int) * n, o, s);
+        FDB_CUDA(cudaStreamSynchronize(s));
+    });
+}
+
+int fdb200_density_detection(const float* knn_dist, const int* knn_idx, int n, int k, int c, const FdB200Opts* opts,
+                             float* densities_out, int* parent_out, int* cores_out, int* num_cores_out,
+                             int* final_k_out)
+{
+    return guarded(opts, nullptr, nullptr, [&](Workspace& ws, const FdB200Opts& o, cudaStream_t s) {
+        FDB_REQUIRE(knn_dist && knn_idx && densities_out && parent_out && cores_out && n >= 2 && k >= 1 && c >= 1,
+                    "fdb200_density_detection: bad arguments");
+        const float* dist = upload_f32(ws.dist, knn_dist, (size_t)n * k, o, s);
+        const int* idx = upload_i32(ws.idx, knn_idx, (size_t)n * k, o, s);
+        FitBuffers b = carve(ws, n, 1);
+        float* den = o.outputs_on_device ? densities_out : ws.den.as<float>(n);
+        int* parent = o.outputs_on_device ? parent_out : ws.parent.as<int>(n);
+        int* cores = o.outputs_on_device ? cores_out : ws.cores.as<int>(n);
+        const int gauss = (o.density_kernel == FDB200_GAUSSIAN) ? 1 : 0;
+        int kk = k;
+        exact_mean(ws, dist, n, kk, b.mean, s);
+        density_from_mean(dist, n, kk, gauss, b.mean, den, s);
+        int nc = dc_detection(ws, idx, den, n, kk, parent, cores, s);
+        while (nc < c) {   // fastdecbase.cpp:186-199
+            if (kk <= 1) throw Error(FDB200_ECORES, "Fit: not enough core points");
+            kk /= 2;
+            exact_mean(ws, dist, n, kk, b.mean, s);
+            density_from_mean(dist, n, kk, gauss, b.mean, den, s);
+            nc = dc_detection(ws, idx, den, n, kk, parent, cores, s);
+        }
+        if (!o.outputs_on_device) {
+            download(densities_out, den, sizeof(float) * n, o, s);
+            download(parent_out, parent, sizeof(int) * n, o, s);
+            download(cores_out, cores, sizeof(int) * nc, o, s);
+        }
+        FDB_CUDA(cudaStreamSynchronize(s));
+        if (num_cores_out) *num_cores_out = nc;
+        if (final_k_out) *final_k_out = kk;
+    });
+}
+
+int fdb200_dc_stage(int stage, const float* data_dev, int n, int d, const float* densities_dev, const int* cores_dev,
+                    int core_nb, int p_lo, int p_hi, const FdB200Opts* opts, uint64_t* best_dev, int* rank_dev)
+{
+    return guarded(opts, nullptr, nullptr, [&](Workspace& ws, const FdB200Opts&, cudaStream_t s) {
+        FDB_REQUIRE(stage == 0 || stage == 1, "fdb200_dc_stage: stage is 0 or 1");
+        FDB_REQUIRE(data_dev && densities_dev && cores_dev && best_dev && (stage == 0 || rank_dev) && core_nb > 0 &&
+                        n > 0 && d > 0 && 0 <= p_lo && p_lo <= p_hi && p_hi <= n,
+                    "fdb200_dc_stage: bad arguments");
+        float* norms = ws.norms.as<float>(n);
+        compute_norms(data_dev, n, n, d, norms, s);
+        dc_stage_range(ws, stage, data_dev, n, n, d, norms, densities_dev, cores_dev, core_nb, p_lo, p_hi, best_dev,
+                       rank_dev, s);
+        FDB_CUDA(cudaStreamSynchronize(s));
+    });
+}
+
+int fdb200_dc_select(const float* densities_dev, const int* cores_dev, int core_nb, const uint64_t* best_dev,
+                     const int* rank_dev, int num_centers, const FdB200Opts* opts, int* core_parent_dev,
+                     int* centers_dev)
+{
+    return guarded(opts, nullptr, nullptr, [&](Workspace& ws, const FdB200Opts&, cudaStream_t s) {
+        FDB_REQUIRE(densities_dev && cores_dev && best_dev && rank_dev && core_parent_dev && centers_dev &&
+                        core_nb > 0 && num_centers > 0,
+                    "fdb200_dc_select: bad arguments");
+        dc_select(ws, densities_dev, cores_dev, core_nb, best_dev, rank_dev, num_centers, core_parent_dev, centers_dev,
+                  s);
         FDB_CUDA(cudaStreamSynchronize(s));
     });
 }

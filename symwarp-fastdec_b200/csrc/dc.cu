@@ -77,6 +77,7 @@ struct DcArgs {
     int ldc, ncores;
     const float* x;
     int ldx, n, d;
+    int p_lo, p_hi;         // the points this call reduces over: [p_lo, p_hi)
     const float* norms;     // all points
     const float* den;       // all points
     const int* cores;       // global index of each core
@@ -89,17 +90,17 @@ __global__ void __launch_bounds__(kT) dc_stage_a_kernel(DcArgs a)
 {
     __shared__ __align__(16) float As[kDC][kBlock];
     __shared__ __align__(16) float Bs[kDC][kBlock];
-    const int c0 = blockIdx.x * kBlock, p0 = blockIdx.y * kBlock;
+    const int c0 = blockIdx.x * kBlock, p0 = a.p_lo + blockIdx.y * kBlock;
     float acc[8][8];
-    core_point_dots(a.xc, a.ldc, a.ncores, a.x, a.ldx, a.n, a.d, c0, p0, As, Bs, acc);
+    core_point_dots(a.xc, a.ldc, a.ncores, a.x, a.ldx, a.p_hi, a.d, c0, p0, As, Bs, acc);
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     float np[8], dp[8];
     int gp[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         gp[j] = p0 + tile_row(j, tx);
-        np[j] = gp[j] < a.n ? a.norms[gp[j]] : 0.0f;
-        dp[j] = gp[j] < a.n ? a.den[gp[j]] : -FLT_MAX;
+        np[j] = gp[j] < a.p_hi ? a.norms[gp[j]] : 0.0f;
+        dp[j] = gp[j] < a.p_hi ? a.den[gp[j]] : -FLT_MAX;
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -110,7 +111,7 @@ __global__ void __launch_bounds__(kT) dc_stage_a_kernel(DcArgs a)
             const float cden = a.den[gc], cn = a.norms[gc];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                if (gp[j] < a.n && cden < dp[j]) {
+                if (gp[j] < a.p_hi && cden < dp[j]) {
                     const uint64_t key = pack_key(exact_d2(cn, np[j], acc[i][j]), gp[j]);
                     best = key < best ? key : best;
                 }
@@ -130,16 +131,16 @@ __global__ void __launch_bounds__(kT) dc_stage_b_kernel(DcArgs a)
 {
     __shared__ __align__(16) float As[kDC][kBlock];
     __shared__ __align__(16) float Bs[kDC][kBlock];
-    const int c0 = blockIdx.x * kBlock, p0 = blockIdx.y * kBlock;
+    const int c0 = blockIdx.x * kBlock, p0 = a.p_lo + blockIdx.y * kBlock;
     float acc[8][8];
-    core_point_dots(a.xc, a.ldc, a.ncores, a.x, a.ldx, a.n, a.d, c0, p0, As, Bs, acc);
+    core_point_dots(a.xc, a.ldc, a.ncores, a.x, a.ldx, a.p_hi, a.d, c0, p0, As, Bs, acc);
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     float np[8];
     int gp[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         gp[j] = p0 + tile_row(j, tx);
-        np[j] = gp[j] < a.n ? a.norms[gp[j]] : 0.0f;
+        np[j] = gp[j] < a.p_hi ? a.norms[gp[j]] : 0.0f;
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -152,7 +153,7 @@ __global__ void __launch_bounds__(kT) dc_stage_b_kernel(DcArgs a)
                 const float cn = a.norms[a.cores[c]];
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
-                    if (gp[j] < a.n && exact_d2(cn, np[j], acc[i][j]) < d2p) ++cnt;
+                    if (gp[j] < a.p_hi && exact_d2(cn, np[j], acc[i][j]) < d2p) ++cnt;
             }
         }
 #pragma unroll
@@ -170,6 +171,13 @@ __global__ void gather_cores_kernel(const float* __restrict__ x, int ldx, int d,
     const int dd = (int)(t / ncores), c = (int)(t % ncores);
     xc[(size_t)dd * ldc + c] = x[(size_t)dd * ldx + cores[c]];
     if (dd == 0) core_den[c] = den[cores[c]];
+}
+
+__global__ void core_den_kernel(const float* __restrict__ den, const int* __restrict__ cores, int ncores,
+                                float* __restrict__ core_den)
+{
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c < ncores) core_den[c] = den[cores[c]];
 }
 
 // dc_cb_split_packed + dc_cb_finalize (dcreductioncuda.cu:113-129, 172-187)
@@ -356,40 +364,99 @@ __global__ void assign_labels_kernel(const int* __restrict__ root, const int* __
 
 }  // namespace
 
+namespace {
+
+// scratch of the DC stages: the gathered core coordinates, dim-major (d x ldc)
+struct DcScratch {
+    int ldc;
+    float* xc;
+    float* core_den;   // written by the gather, unused by the stages
+};
+
+DcScratch dc_scratch(Workspace& ws, int core_nb, int d)
+{
+    DcScratch t;
+    t.ldc = ((core_nb + kBlock - 1) / kBlock) * kBlock;
+    const size_t xc_bytes = ((sizeof(float) * (size_t)t.ldc * d + 255) & ~size_t(255));
+    // also room for dc_select's per-core scratch, which reuses this buffer once the stages are done
+    const size_t sel_bytes = 3 * (((size_t)t.ldc * 4 + 255) & ~size_t(255)) + (size_t)t.ldc + 256;
+    char* base = (char*)ws.dc_tmp.ensure(std::max(xc_bytes + sizeof(float) * (size_t)t.ldc + 256, sel_bytes));
+    t.xc = (float*)base;
+    t.core_den = (float*)(base + xc_bytes);
+    return t;
+}
+
+void gather_cores(const DcScratch& t, const float* x, int ldx, int d, const float* den, const int* cores, int core_nb,
+                  cudaStream_t s)
+{
+    FDB_CUDA(cudaMemsetAsync(t.xc, 0, sizeof(float) * (size_t)t.ldc * d, s));
+    const size_t tot = (size_t)core_nb * d;
+    gather_cores_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(x, ldx, d, cores, core_nb, t.ldc, t.xc, den,
+                                                                       t.core_den);
+    FDB_LAUNCHED();
+}
+
+void launch_stage(int stage, const DcScratch& t, const float* x, int ldx, int n, int d, const float* norms,
+                  const float* den, const int* cores, int core_nb, int p_lo, int p_hi, uint64_t* best, int* rank,
+                  cudaStream_t s)
+{
+    if (p_hi <= p_lo) return;
+    DcArgs a{t.xc, t.ldc, core_nb, x, ldx, n, d, p_lo, p_hi, norms, den, cores, best, rank};
+    dim3 grid((core_nb + kBlock - 1) / kBlock, (p_hi - p_lo + kBlock - 1) / kBlock);
+    if (stage == 0) dc_stage_a_kernel<<<grid, kT, 0, s>>>(a);
+    else dc_stage_b_kernel<<<grid, kT, 0, s>>>(a);
+    FDB_LAUNCHED();
+}
+
+}  // namespace
+
 void dc_reduction(Workspace& ws, const float* x, int ldx, int n, int d, const float* norms, const float* den,
                   const int* cores, int core_nb, int num_centers, int* core_parent, int* centers,
                   cudaStream_t s)
 {
     FDB_REQUIRE(core_nb > 0 && num_centers > 0 && n > 0 && d > 0, "DC reduction: empty input");
-    const int ldc = ((core_nb + kBlock - 1) / kBlock) * kBlock;
-    // scratch layout
-    const size_t xc_bytes = sizeof(float) * (size_t)ldc * d;
-    const size_t need = xc_bytes + (sizeof(uint64_t) + 3 * sizeof(float) + 2 * sizeof(int) + 1) * (size_t)ldc + 1024;
-    char* base = (char*)ws.dc_tmp.ensure(need);
-    float* xc = (float*)base;
-    uint64_t* best = (uint64_t*)(base + ((xc_bytes + 255) & ~size_t(255)));
-    float* core_den = (float*)(best + ldc);
-    float* delta = core_den + ldc;
-    int* rank = (int*)(delta + ldc);
-    unsigned char* chosen = (unsigned char*)(rank + ldc);
-
-    FDB_CUDA(cudaMemsetAsync(xc, 0, xc_bytes, s));
-    const size_t tot = (size_t)core_nb * d;
-    gather_cores_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(x, ldx, d, cores, core_nb, ldc, xc, den,
-                                                                       core_den);
-    FDB_LAUNCHED();
+    const DcScratch t = dc_scratch(ws, core_nb, d);
+    uint64_t* best = ws.dc_sel.as<uint64_t>((size_t)2 * core_nb + 64);   // best keys, then ranks
+    int* rank = reinterpret_cast<int*>(best + core_nb);
+    gather_cores(t, x, ldx, d, den, cores, core_nb, s);
     FDB_CUDA(cudaMemsetAsync(best, 0xFF, sizeof(uint64_t) * core_nb, s));
     FDB_CUDA(cudaMemsetAsync(rank, 0, sizeof(int) * core_nb, s));
-    DcArgs a{xc, ldc, core_nb, x, ldx, n, d, norms, den, cores, best, rank};
-    dim3 grid((core_nb + kBlock - 1) / kBlock, (n + kBlock - 1) / kBlock);
-    dc_stage_a_kernel<<<grid, kT, 0, s>>>(a);
+    launch_stage(0, t, x, ldx, n, d, norms, den, cores, core_nb, 0, n, best, rank, s);
+    launch_stage(1, t, x, ldx, n, d, norms, den, cores, core_nb, 0, n, best, rank, s);
+    dc_select(ws, den, cores, core_nb, best, rank, num_centers, core_parent, centers, s);
+}
+
+void dc_stage_range(Workspace& ws, int stage, const float* x, int ldx, int n, int d, const float* norms,
+                    const float* den, const int* cores, int core_nb, int p_lo, int p_hi, uint64_t* best, int* rank,
+                    cudaStream_t s)
+{
+    FDB_REQUIRE(core_nb > 0 && n > 0 && d > 0 && 0 <= p_lo && p_lo <= p_hi && p_hi <= n,
+                "DC reduction stage: bad core count or point range");
+    const DcScratch t = dc_scratch(ws, core_nb, d);
+    gather_cores(t, x, ldx, d, den, cores, core_nb, s);
+    if (stage == 0) FDB_CUDA(cudaMemsetAsync(best, 0xFF, sizeof(uint64_t) * core_nb, s));
+    else FDB_CUDA(cudaMemsetAsync(rank, 0, sizeof(int) * core_nb, s));
+    launch_stage(stage, t, x, ldx, n, d, norms, den, cores, core_nb, p_lo, p_hi, best, rank, s);
+}
+
+void dc_select(Workspace& ws, const float* den, const int* cores, int core_nb, const uint64_t* best, const int* rank_in,
+               int num_centers, int* core_parent, int* centers, cudaStream_t s)
+{
+    FDB_REQUIRE(core_nb > 0 && num_centers > 0, "DC selection: empty input");
+    // per core: density, delta, a working copy of the rank (finalize fills it), chosen flag -- after
+    // the stages' best keys and ranks, which may live in the same buffer
+    const size_t c4 = ((size_t)core_nb * 4 + 255) & ~size_t(255);
+    char* base = (char*)ws.dc_tmp.ensure(3 * c4 + (size_t)core_nb + 256);
+    float* core_den = (float*)base;
+    float* delta = (float*)(base + c4);
+    int* rank = (int*)(base + 2 * c4);
+    unsigned char* chosen = (unsigned char*)(base + 3 * c4);
+    core_den_kernel<<<(core_nb + 255) / 256, 256, 0, s>>>(den, cores, core_nb, core_den);
     FDB_LAUNCHED();
-    dc_stage_b_kernel<<<grid, kT, 0, s>>>(a);
-    FDB_LAUNCHED();
+    FDB_CUDA(cudaMemcpyAsync(rank, rank_in, sizeof(int) * core_nb, cudaMemcpyDeviceToDevice, s));
     dc_finalize_kernel<<<(core_nb + 255) / 256, 256, 0, s>>>(best, rank, core_nb, core_parent, delta);
     FDB_LAUNCHED();
-    select_centers_kernel<<<1, 1024, 0, s>>>(core_den, delta, rank, cores, core_nb, num_centers, chosen,
-                                             centers);
+    select_centers_kernel<<<1, 1024, 0, s>>>(core_den, delta, rank, cores, core_nb, num_centers, chosen, centers);
     FDB_LAUNCHED();
 }
 

@@ -60,7 +60,7 @@ struct Workspace {
     cudaStream_t own_stream = nullptr;
     int* pinned = nullptr;                 // small pinned host scratch for flags / counters
     DevBuf data, norms, lists, thr, fthr, cand, cnt, flags;
-    DevBuf dist, idx, den, parent, cores, scan, mean_tmp, dc_tmp, labels_tmp, misc, ops, misc2;
+    DevBuf dist, idx, den, parent, cores, scan, mean_tmp, dc_tmp, dc_sel, labels_tmp, misc, ops, misc2;
     void release_all();
 };
 
@@ -91,6 +91,7 @@ struct KnnConfig {
     int precision = FDB200_FP32;
     int engine = FDB200_ENGINE_AUTO;
     int shard_rank = 0, shard_count = 1;
+    int block_lo = -1, block_hi = -1;   // explicit row-block range of the shard (-1: from rank / count)
     int cand_capacity = 0;
 };
 
@@ -160,6 +161,16 @@ void dc_reduction(Workspace& ws, const float* x, int ldx, int n, int d, const fl
                   int* core_parent, int* centers, cudaStream_t s);
 void scatter_core_parents(const int* cores, const int* core_parent, int core_nb, int* parent,
                           cudaStream_t s);
+// The same reduction split by point ranges (for sharding it across GPUs): stage 0 writes best[c] = the
+// lexicographic minimum (d2 bits << 32 | index) over the strictly denser points of [p_lo, p_hi)
+// (UINT64_MAX if none); stage 1 writes rank[c] = the points of [p_lo, p_hi) closer to core c than the
+// parent in best[c]. Keys of several ranges combine by minimum, ranks by sum; dc_select then finishes
+// (parents, delta, fills, center selection) from the combined arrays.
+void dc_stage_range(Workspace& ws, int stage, const float* x, int ldx, int n, int d, const float* norms,
+                    const float* den, const int* cores, int core_nb, int p_lo, int p_hi, uint64_t* best, int* rank,
+                    cudaStream_t s);
+void dc_select(Workspace& ws, const float* den, const int* cores, int core_nb, const uint64_t* best, const int* rank,
+               int num_centers, int* core_parent, int* centers, cudaStream_t s);
 // labels on the device; throws Error(FDB200_ECYCLE) if the parent graph has a cycle
 void final_cluster(Workspace& ws, const int* parent, int n, const int* centers, int c, int* labels,
                    cudaStream_t s);

@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kSimtThreads, 2) knn_tile_simt(TileRound r)
                 if (mask & (1u << j)) append_at(r, gi[i], slot++, pack_key(exact_d2(nq[i], nr[j], acc[i][j]), gj[j]));
         }
     }
-    if (r.diag) return;   // diagonal units see both orders of every pair as rows
+    if (r.diag || r.rows_only) return;   // diagonal and rows-only units update their row block only
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         if (gj[j] >= r.n) continue;
@@ -499,8 +499,14 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
                 "bad shard_rank / shard_count");
     KnnResult res;
     const int T = (n + kBlock - 1) / kBlock;
-    const int b_lo = (int)((long long)T * cfg.shard_rank / cfg.shard_count);
-    const int b_hi = (int)((long long)T * (cfg.shard_rank + 1) / cfg.shard_count);
+    int b_lo = (int)((long long)T * cfg.shard_rank / cfg.shard_count);
+    int b_hi = (int)((long long)T * (cfg.shard_rank + 1) / cfg.shard_count);
+    if (cfg.block_lo >= 0 || cfg.block_hi >= 0) {
+        FDB_REQUIRE(0 <= cfg.block_lo && cfg.block_lo <= cfg.block_hi && cfg.block_hi <= T,
+                    "shard_block_lo / shard_block_hi must satisfy 0 <= lo <= hi <= ceil(n / 128)");
+        b_lo = cfg.block_lo;
+        b_hi = cfg.block_hi;
+    }
     const int nb = b_hi - b_lo;
     // admissions per round have a fat right tail (the list's k-th key is itself a random order
     // statistic), so rounds are sized for about a quarter of the buffer
@@ -557,7 +563,7 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     // change in the merges of rounds that completed. Host stalls between launches therefore do not
     // leave the device idle.
     struct Planned {
-        int diag, delta0, ndelta, units, engine;
+        int diag, delta0, ndelta, units, engine, rows_only;
         double seen;   // the `seen` estimate before the round
     };
     std::vector<Planned> plan;
@@ -596,16 +602,20 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
             // With the automatic engine, the first rounds run on the exact SIMT tiles: they offer every
             // point few, mostly admissible candidates (its thresholds are still loose), so nearly every
             // pair would be refined after the TF32 filter anyway (measured at the headline size: the
-            // diagonal and the first three offset rounds take 28 ms instead of 67 ms). An explicit
-            // tcgen05 request, and a sharded run (its rows-only bookkeeping needs one engine), keep
-            // tcgen05 for every round.
+            // diagonal and the first three offset rounds take 28 ms instead of 67 ms). A sharded run
+            // gives them rows-only SIMT tiles (each ordered block pair once, its own rows updated), so
+            // a shard's lists are final without an exchange, as with its tcgen05 rounds. An explicit
+            // tcgen05 request keeps tcgen05 for every round.
             pl.engine = (cfg.engine == FDB200_ENGINE_AUTO && engine == FDB200_ENGINE_TCGEN05 &&
-                         cfg.shard_count == 1 && (pl.diag || pl.ndelta <= kSimtRoundMaxOffsets))
+                         (pl.diag || pl.ndelta <= kSimtRoundMaxOffsets))
                             ? FDB200_ENGINE_SIMT
                             : engine;
+            pl.rows_only = (pl.engine == FDB200_ENGINE_SIMT && engine == FDB200_ENGINE_TCGEN05 && nb < T) ? 1 : 0;
+            if (pl.rows_only && !pl.diag) pl.units = 2 * nb * pl.ndelta;
             plan.push_back(pl);
             const int slot = (int)plan.size();
             r.diag = pl.diag;
+            r.rows_only = pl.rows_only;
             r.delta0 = pl.delta0;
             r.ndelta = pl.ndelta;
             r.tag = slot;
@@ -613,9 +623,11 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
             launch_tile_round(r, pl.units, pl.engine, cfg.precision, s);
             FDB_CUDA(cudaEventRecord(ev.get(2 * slot + 1), s));
             if (trace) FDB_CUDA(cudaEventRecord(m0, s));
-            // a tcgen05 round appends only to this shard's rows; a SIMT round to any point
-            const int plo = pl.engine == FDB200_ENGINE_TCGEN05 ? b_lo * kBlock : 0;
-            const int phi = pl.engine == FDB200_ENGINE_TCGEN05 ? std::min(n, b_hi * kBlock) : n;
+            // a tcgen05 or rows-only round appends only to this shard's rows; a symmetric SIMT round to
+            // any point
+            const bool own_rows = pl.engine == FDB200_ENGINE_TCGEN05 || pl.rows_only;
+            const int plo = own_rows ? b_lo * kBlock : 0;
+            const int phi = own_rows ? std::min(n, b_hi * kBlock) : n;
             if (k <= kSortedMergeMaxK && cap <= 512)
                 knn_merge_sorted_kernel<<<(phi - plo + kSortedMergeWarps - 1) / kSortedMergeWarps, kSortedMergeWarps * 32, 0, s>>>(
                     lists, thr, U, norms, cand, cnt, plo, phi, k, cap, d, kp, exact, admitted, fold.aimg, fold.ntf, ovf);

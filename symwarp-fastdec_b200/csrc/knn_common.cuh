@@ -31,6 +31,9 @@ struct TileRound {
     int T;                   // blocks in the triangle
     int b_lo, nb;            // this shard's row blocks
     int diag;                // 1: diagonal units (B, B), row side only
+    int rows_only;           // SIMT tiles: 1 = each unit updates its row block only, and the round covers
+                             // the offsets in both directions (a shard's rows get every candidate
+                             // without updating other shards' points); 0 = symmetric units
     int delta0;              // first block offset of the round
     int ndelta;              // block offsets in the round
     unsigned long long* counters;   // optional tcgen05 diagnostics (FDB200_TRACE=1), else null
@@ -41,6 +44,20 @@ __device__ __forceinline__ bool decode_unit(const TileRound& r, int u, int& B, i
     if (r.diag) {
         B = r.b_lo + u;
         R = B;
+        return true;
+    }
+    if (r.rows_only) {
+        // units [0, nb * ndelta): R = B + delta; [nb * ndelta, 2 nb * ndelta): R = B - delta; with an
+        // even block count the offset T/2 reaches the same block both ways, so its second copy goes
+        const int per = r.nb * r.ndelta;
+        const int back = u >= per ? 1 : 0;
+        const int v = u - back * per;
+        const int dl = r.delta0 + v / r.nb;
+        B = r.b_lo + v % r.nb;
+        if (back && (r.T & 1) == 0 && dl == r.T / 2) return false;
+        R = back ? B - dl : B + dl;
+        if (R >= r.T) R -= r.T;
+        if (R < 0) R += r.T;
         return true;
     }
     const int dl = r.delta0 + u / r.nb;

@@ -44,7 +44,8 @@ class Opts(ctypes.Structure):
                 ("density_kernel", ctypes.c_int), ("engine", ctypes.c_int),
                 ("inputs_on_device", ctypes.c_int), ("outputs_on_device", ctypes.c_int),
                 ("shard_rank", ctypes.c_int), ("shard_count", ctypes.c_int),
-                ("cand_capacity", ctypes.c_int), ("stream", ctypes.c_void_p)]
+                ("cand_capacity", ctypes.c_int), ("stream", ctypes.c_void_p),
+                ("shard_block_lo", ctypes.c_int), ("shard_block_hi", ctypes.c_int)]
 
 
 class Stats(ctypes.Structure):
@@ -65,7 +66,8 @@ EXPORTS = ["fdb200_opts_init", "fdb200_last_error", "fdb200_abi_version", "fdb20
            "fdb200_knn_partial", "fdb200_merge_lists", "fdb200_lists_to_knn", "fdb200_fit_from_knn",
            "fdb200_release", "fdb200_density_noalloc", "fdb200_csv_shape", "fdb200_read_csv",
            "fdb200_write_csv", "fdb200_fbin_shape", "fdb200_read_fbin", "fdb200_write_fbin", "fdb200_knn_graph_save",
-           "fdb200_knn_graph_shape", "fdb200_knn_graph_load"]
+           "fdb200_knn_graph_shape", "fdb200_knn_graph_load", "fdb200_density_detection", "fdb200_dc_stage",
+           "fdb200_dc_select"]
 
 _lib = None
 
@@ -108,6 +110,9 @@ def lib():
         L.fdb200_knn_graph_save.argtypes = [cp, vp, vp, i, i, i]
         L.fdb200_knn_graph_shape.argtypes = [cp, ipp, ipp, ipp]
         L.fdb200_knn_graph_load.argtypes = [cp, i, i, vp, vp]
+        L.fdb200_density_detection.argtypes = [vp, vp, i, i, i, op, vp, vp, vp, ipp, ipp]
+        L.fdb200_dc_stage.argtypes = [i, vp, i, i, vp, vp, i, i, i, op, vp, vp]
+        L.fdb200_dc_select.argtypes = [vp, vp, i, vp, vp, i, op, vp, vp]
         _lib = L
     return _lib
 
@@ -116,7 +121,7 @@ _CUDA_STREAM_LEGACY = 0x1   # cudaStreamLegacy
 
 
 def make_opts(device=0, precision="fp32", density="laplacian", engine="auto", on_device=False,
-              shard=(0, 1), cand_capacity=0, stream=None):
+              shard=(0, 1), cand_capacity=0, stream=None, blocks=None):
     o = Opts()
     lib().fdb200_opts_init(ctypes.byref(o))
     o.device = int(device)
@@ -126,6 +131,8 @@ def make_opts(device=0, precision="fp32", density="laplacian", engine="auto", on
     o.inputs_on_device = o.outputs_on_device = int(bool(on_device))
     o.shard_rank, o.shard_count = int(shard[0]), int(shard[1])
     o.cand_capacity = int(cand_capacity)
+    if blocks is not None:   # explicit shard: row blocks [blocks[0], blocks[1])
+        o.shard_block_lo, o.shard_block_hi = int(blocks[0]), int(blocks[1])
     # stream: None = the library's own stream; an integer handle runs the call on that CUDA stream.
     # Handle 0 is the legacy default stream (torch's default stream reports 0); the ABI reserves a
     # NULL stream for "the library's own", so it is passed as cudaStreamLegacy.
@@ -337,6 +344,38 @@ def fit_from_knn_device(x_dm, dist, idx, k, c, centers, labels, densities=None, 
                                      _ptr(centers), _ptr(labels),
                                      _ptr(densities) if densities is not None else None, ctypes.byref(st)))
     return st.as_dict()
+
+
+def density_detection_device(dist, idx, k, c, den, parent, cores, stream=None, device=0, **kw):
+    """Density + DC detection with the k-halving retry on device tensors (rank-major (>= k, n) dist / idx;
+    den (n,) float32, parent (n,) int32, cores (n,) int32 outputs). Returns (num_cores, final_k)."""
+    n = dist.shape[1]
+    nc, fk = ctypes.c_int(0), ctypes.c_int(0)
+    o = make_opts(on_device=True, stream=stream, device=device, **kw)
+    _check(lib().fdb200_density_detection(_ptr(dist), _ptr(idx), n, k, c, ctypes.byref(o), _ptr(den), _ptr(parent),
+                                          _ptr(cores), ctypes.byref(nc), ctypes.byref(fk)))
+    return nc.value, fk.value
+
+
+def dc_stage_device(stage, x_dm, den, cores, core_nb, p_lo, p_hi, best, rank=None, stream=None):
+    """One stage of the DC reduction over the points [p_lo, p_hi) (device tensors; best: (core_nb,) int64
+    holding packed uint64 keys, rank: (core_nb,) int32)."""
+    d, n = x_dm.shape
+    o = make_opts(on_device=True, stream=stream, device=x_dm.device.index or 0)
+    _check(lib().fdb200_dc_stage(int(stage), _ptr(x_dm), n, d, _ptr(den), _ptr(cores), int(core_nb), int(p_lo),
+                                 int(p_hi), ctypes.byref(o), _ptr(best), _ptr(rank) if rank is not None else None))
+
+
+def dc_select_device(den, cores, core_nb, best, rank, c, core_parent, centers, stream=None, device=0):
+    o = make_opts(on_device=True, stream=stream, device=device)
+    _check(lib().fdb200_dc_select(_ptr(den), _ptr(cores), int(core_nb), _ptr(best), _ptr(rank), int(c),
+                                  ctypes.byref(o), _ptr(core_parent), _ptr(centers)))
+
+
+def final_cluster_device(parent, centers, labels, stream=None, device=0):
+    o = make_opts(on_device=True, stream=stream, device=device)
+    _check(lib().fdb200_final_cluster(_ptr(parent), parent.shape[0], _ptr(centers), centers.shape[0],
+                                      ctypes.byref(o), _ptr(labels)))
 
 
 def release(device=0):

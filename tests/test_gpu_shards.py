@@ -23,16 +23,18 @@ def _lists(fdb, xd, k, shard, engine, precision="fp32"):
 
 
 @pytest.mark.parametrize("world", [2, 3, 8])
-@pytest.mark.parametrize("engine", ["tcgen05", "simt"])
+@pytest.mark.parametrize("engine", ["tcgen05", "auto", "simt"])
 def test_shards_on_one_gpu_equal_the_unsharded_lists(fdb, world, engine):
+    """auto: a shard's dense first rounds run on rows-only SIMT tiles, the rest on tcgen05 -- its own
+    rows are final either way"""
     import torch
     n, k = 40_000, 45
     xd = torch.from_numpy(embedding_cloud(n=n, d=50, seed=31)).cuda()
     full, _ = _lists(fdb, xd, k, (0, 1), engine)
     parts = [_lists(fdb, xd, k, (r, world), engine) for r in range(world)]
-    assert all(st["engine_used"] == (2 if engine == "tcgen05" else 1) for _, st in parts)
+    assert all(st["engine_used"] == (1 if engine == "simt" else 2) for _, st in parts)
     assert sum(st["pairs"] for _, st in parts) == n * (n - 1) // 2
-    if engine == "tcgen05":
+    if engine != "simt":
         got = np.concatenate([p[a:b] for (p, _), (a, b) in zip(parts, block_ranges(n, world))])
     else:
         # the owners' merge of the exchanged partial lists, by the library (fdb200_merge_lists), for
@@ -46,6 +48,25 @@ def test_shards_on_one_gpu_equal_the_unsharded_lists(fdb, world, engine):
         # and the same selection restated on the host
         assert np.array_equal(np.sort(np.concatenate([p for p, _ in parts], axis=1), axis=1)[:, :k], full)
     assert np.array_equal(got, full)
+
+
+def test_weighted_shards_with_overflow_reruns_stay_exact(fdb):
+    """explicit (uneven) row-block ranges, rows-only SIMT rounds that overflow a small candidate buffer
+    and are re-planned in halves: the shards' own rows still equal the unsharded lists"""
+    import torch
+    from fastdec_b200.multigpu import block_split
+    n, k, world = 6000, 8, 3
+    x = np.zeros((2, n), np.float32)
+    x[0] = np.random.default_rng(1).integers(0, 2, n)
+    xd = torch.from_numpy(x).cuda()
+    full, _ = _lists(fdb, xd, k, (0, 1), "simt")
+    got = []
+    for r, (b0, b1) in enumerate(block_split(n, world, 0.5)):
+        out = torch.empty((n, k), dtype=torch.int64, device=xd.device)
+        st = fdb.knn_partial_device(xd, k, out, (r, world), engine="auto", cand_capacity=256, blocks=(b0, b1))
+        torch.cuda.synchronize()
+        got.append(out.cpu().numpy().view(np.uint64)[128 * b0:min(n, 128 * b1)])
+    assert np.array_equal(np.concatenate(got), full)
 
 
 def test_shards_at_128_dimensions_split_k(fdb):

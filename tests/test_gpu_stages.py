@@ -82,3 +82,48 @@ def test_final_cluster_detects_cycles(fdb):
     with pytest.raises(fdb.FastDecError) as e:
         fdb.final_cluster(parent, np.array([3], np.int32))
     assert e.value.code == -5
+
+
+@pytest.mark.parametrize("ranges", [3, 8])
+def test_sharded_dc_reduction_stages_equal_the_whole(fdb, oracle, ranges):
+    """fdb200_dc_stage over disjoint point ranges, combined by minimum (stage A keys) and sum (stage B
+    ranks) as the multi-GPU fit combines them, then fdb200_dc_select: the same core parents and
+    centers as fdb200_dc_reduction and the reference's host stages. Also fdb200_density_detection
+    against the reference (densities, cores, final k)."""
+    import torch
+    from fastdec_b200.multigpu import owner_ranges
+    x = ds.embedding_cloud(n=30_000, d=50, seed=41)
+    n, k, c = x.shape[1], 20, 12
+    dist, idx, _ = fdb.knn(x, k)
+    dd, di = torch.from_numpy(dist).cuda(), torch.from_numpy(idx).cuda()
+    den = torch.empty(n, dtype=torch.float32, device="cuda")
+    parent = torch.empty(n, dtype=torch.int32, device="cuda")
+    cores = torch.empty(n, dtype=torch.int32, device="cuda")
+    nc, fk = fdb.density_detection_device(dd, di, k, c, den, parent, cores)
+    ref = oracle.ref_fit_from_knn(x, dist, idx, c)
+    assert fk == ref["final_k"] and nc == ref["num_cores"] and nc > c
+    assert np.array_equal(den.cpu().numpy().view(np.uint32), ref["densities"].view(np.uint32))
+    assert np.array_equal(cores[:nc].cpu().numpy(), ref["cores"])
+    xd = torch.from_numpy(x).cuda()
+    cr = cores[:nc].contiguous()
+    best = []
+    for a, b in owner_ranges(n, ranges):
+        t = torch.empty(nc, dtype=torch.int64, device="cuda")
+        fdb.dc_stage_device(0, xd, den, cr, nc, a, b, t)
+        best.append(t.cpu().numpy().view(np.uint64))
+    comb = torch.from_numpy(np.minimum.reduce(best).view(np.int64).copy()).cuda()
+    rk = np.zeros(nc, np.int64)
+    for a, b in owner_ranges(n, ranges):
+        t = torch.empty(nc, dtype=torch.int32, device="cuda")
+        fdb.dc_stage_device(1, xd, den, cr, nc, a, b, comb, t)
+        rk += t.cpu().numpy()
+    rkd = torch.from_numpy(rk.astype(np.int32)).cuda()
+    cp = torch.empty(nc, dtype=torch.int32, device="cuda")
+    ctr = torch.empty(c, dtype=torch.int32, device="cuda")
+    fdb.dc_select_device(den, cr, nc, comb, rkd, c, cp, ctr)
+    wcp, wctr = fdb.dc_reduction(x, den.cpu().numpy(), cr.cpu().numpy(), c)
+    assert np.array_equal(cp.cpu().numpy(), wcp) and np.array_equal(ctr.cpu().numpy(), wctr)
+    assert ctr.cpu().numpy().tolist() == ref["centers"].tolist()
+    p = parent.cpu().numpy()
+    p[cr.cpu().numpy()] = cp.cpu().numpy()
+    assert np.array_equal(p, ref["parents"])

@@ -102,6 +102,20 @@ def test_block_ranges_follow_the_kernel_row_block_split():
             assert all(a == min(n, 128 * (T * r // world)) for r, (a, _) in enumerate(rng))
 
 
+def test_weighted_block_split_gives_rank_0_less():
+    from fastdec_b200.multigpu import block_split
+    for n in (129, 5000, 1_291_147):
+        T = (n + 127) // 128
+        for world in (2, 3, 8):
+            for share in (0.5, 0.9, 0.96):
+                sp = block_split(n, world, share)
+                assert sp[0][0] == 0 and sp[-1][1] == T
+                assert all(sp[i][1] == sp[i + 1][0] for i in range(world - 1))
+                sizes = [b - a for a, b in sp]
+                assert abs(sizes[0] - share * T / world) <= 0.5 + 1e-9
+                assert max(sizes[1:]) - min(sizes[1:]) <= 1
+
+
 def _gather_worker(rank, world, port, n, k, q):
     from fastdec_b200.multigpu import block_ranges
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -169,3 +183,55 @@ def test_gather_with_a_dead_peer_fails_instead_of_hanging():
         p.join(timeout=60)
     assert results[1] == "left"
     assert results[0].startswith("error:")
+
+
+def test_signed_key_mapping_keeps_the_unsigned_order():
+    from fastdec_b200.multigpu import keys_to_signed
+    rng = np.random.default_rng(5)
+    d2 = np.abs(rng.standard_normal(2000)).astype(np.float32)
+    d2[:3] = [0.0, np.float32(np.inf), np.float32(3.4e38)]
+    keys = (d2.view(np.uint32).astype(np.uint64) << np.uint64(32)) | rng.integers(0, 2 ** 31, 2000).astype(np.uint64)
+    keys[5] = EMPTY
+    s = keys_to_signed(torch.from_numpy(keys.view(np.int64).copy())).numpy()
+    assert np.array_equal(keys[np.argsort(keys, kind="stable")], keys[np.argsort(s, kind="stable")])
+    assert s[5] == np.iinfo(np.int64).max
+    assert np.array_equal(keys_to_signed(torch.from_numpy(s.copy())).numpy().view(np.uint64), keys)
+
+
+def _dc_combine_worker(rank, world, port, q):
+    from fastdec_b200.multigpu import all_reduce_keys_min
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(3)
+        parts = []
+        for s in range(world):   # every rank draws every rank's partial keys, keeps its own
+            d2 = np.abs(rng.standard_normal(300)).astype(np.float32)
+            k = (d2.view(np.uint32).astype(np.uint64) << np.uint64(32)) | rng.integers(0, 10 ** 6, 300).astype(np.uint64)
+            k[rng.random(300) < 0.3] = EMPTY   # cores with no denser point in this rank's range
+            parts.append(k)
+        mine = torch.from_numpy(parts[rank].view(np.int64).copy())
+        all_reduce_keys_min(mine)
+        assert np.array_equal(mine.numpy().view(np.uint64), np.minimum.reduce(parts))
+        q.put((rank, "ok"))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_dc_partial_keys_combine_by_unsigned_min_over_ranks():
+    """The sharded DC reduction's stage-A keys (packed uint64 in int64 tensors, UINT64_MAX = no denser
+    point) combine across ranks by an all-reduce MIN after the signed mapping."""
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dc_combine_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert results == {r: "ok" for r in range(world)}
