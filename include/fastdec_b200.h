@@ -210,6 +210,19 @@ int fdb200_dc_select(const float* densities_dev, const int* cores_dev, int core_
                      const int* rank_dev, int num_centers, const FdB200Opts* opts, int* core_parent_dev,
                      int* centers_dev);
 
+/*
+ * DIAGNOSTICS: audit of the tcgen05 filter's margin on a small problem (n <= 16384; device pointers). For
+ * every point i the threshold thr_d2_dev[i] (a squared distance, e.g. the point's exact k-th neighbour)
+ * is folded into the row operand exactly as the list merge folds a list's threshold; then one
+ * tcgen05.mma per 128 x 256 tile computes acc_dev[i * n + j] = the FP32 accumulation of
+ * |x~_i - x~_j|^2 - V_i, which the filter keeps a pair for iff it is negative. bound_dev[i] = V_i;
+ * arows_dev / brows_dev: the TF32 operand rows (n x K each, K = *kp_out) the MMA consumed, so a test can
+ * form the exact sum and measure the accumulation error against the error model the margin assumes.
+ * No counterpart in the reference (its TF32 path has no rigorous filter).
+ */
+int fdb200_debug_tc_filter(const float* data_dev, int n, int d, const float* thr_d2_dev, const FdB200Opts* opts,
+                           float* acc_dev, float* bound_dev, float* arows_dev, float* brows_dev, int* kp_out);
+
 /* Frees the library's cached device workspace on opts->device. */
 int fdb200_release(const FdB200Opts* opts);
 

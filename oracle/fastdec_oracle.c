@@ -50,6 +50,18 @@ float or_pair_d2(const float* x, int n, int d, const float* norms, int i, int j)
     return finish_d2(norms[i], norms[j], dot);
 }
 
+/* every ordered pair's d2 (out[i * n + j], the diagonal included) by the same fmaf chain and finish:
+   test support for small n */
+void or_pair_d2_all(const float* x, int n, int d, float* out)
+{
+    float* norms = (float*)malloc(sizeof(float) * (size_t)n);
+    if (!norms) return;
+    or_norms(x, n, d, norms);
+    for (int i = 0; i < n; ++i)
+        for (int j = 0; j < n; ++j) out[(size_t)i * n + j] = or_pair_d2(x, n, d, norms, i, j);
+    free(norms);
+}
+
 /* ---- bounded max-heap of packed keys with strict admission (symtriknncuda.cu:104-136) ---- */
 static void heap_offer(uint64_t* h, int k, uint64_t key)
 {

@@ -36,6 +36,8 @@ void or_norms(const float* x_dm, int n, int d, float* norms);
 
 /* d2 of one pair, exactly as the reference FDS tile computes it */
 float or_pair_d2(const float* x_dm, int n, int d, const float* norms, int i, int j);
+/* every ordered pair's d2 into out[i * n + j] (test support, small n) */
+void or_pair_d2_all(const float* x_dm, int n, int d, float* out);
 
 /* full exact self-kNN; outputs rank-major sqrt'd distances and indices (k * n each).
    Returns 0 on success, -1 on bad arguments (k >= n etc.). */

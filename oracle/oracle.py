@@ -53,6 +53,7 @@ def lib():
         L.or_pair_d2.argtypes = [_f32p, c_int, c_int, _f32p, c_int, c_int]
         L.or_pair_d2.restype = ctypes.c_float
         L.or_knn.argtypes = [_f32p, c_int, c_int, c_int, c_int, _f32p, _i32p]
+        L.or_pair_d2_all.argtypes = [_f32p, c_int, c_int, _f32p]
         L.or_knn_rows.argtypes = [_f32p, c_int, c_int, c_int, _i32p, c_int, c_int, _f32p, _i32p]
         L.or_mean_knn_dist.argtypes = [_f32p, c_int, c_int]
         L.or_mean_knn_dist.restype = c_double
@@ -83,6 +84,16 @@ def norms(x_dm):
     d, n = x.shape
     out = np.empty(n, np.float32)
     lib().or_norms(x, n, d, out)
+    return out
+
+
+def pair_d2_all(x_dm):
+    """(n, n) squared distances of every ordered pair as the reference computes them (fmaf-chain dot,
+    symtriknnfds.h:23-26). Small n only."""
+    x = _dm(x_dm)
+    d, n = x.shape
+    out = np.empty((n, n), np.float32)
+    lib().or_pair_d2_all(x, n, d, out)
     return out
 
 

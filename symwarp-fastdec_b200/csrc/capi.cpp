@@ -431,6 +431,18 @@ int fdb200_lists_to_knn(const uint64_t* lists_dev, int n, int k, const FdB200Opt
     });
 }
 
+int fdb200_debug_tc_filter(const float* data_dev, int n, int d, const float* thr_d2_dev, const FdB200Opts* opts,
+                           float* acc_dev, float* bound_dev, float* arows_dev, float* brows_dev, int* kp_out)
+{
+    return guarded(opts, nullptr, nullptr, [&](Workspace& ws, const FdB200Opts& o, cudaStream_t s) {
+        FDB_REQUIRE(data_dev && thr_d2_dev && acc_dev && bound_dev && arows_dev && brows_dev && n >= 2 && d >= 1,
+                    "fdb200_debug_tc_filter: bad arguments");
+        FDB_REQUIRE(n <= 16384, "fdb200_debug_tc_filter: n is limited to 16384 (an n x n output)");
+        tc_filter_audit(ws, data_dev, n, d, thr_d2_dev, o.precision, acc_dev, bound_dev, arows_dev, brows_dev, s);
+        if (kp_out) *kp_out = ((d + 6 + 7) / 8) * 8;   // K of the operand rows (tc_kp)
+    });
+}
+
 int fdb200_release(const FdB200Opts* opts)
 {
     return guarded(opts, nullptr, nullptr, [&](Workspace& ws, const FdB200Opts&, cudaStream_t s) {

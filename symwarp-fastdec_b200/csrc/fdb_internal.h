@@ -126,6 +126,11 @@ struct TcFold {
 TcFold tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const float* norms, const float* U,
                   const uint64_t* thr, cudaStream_t s);
 
+// filter audit (diagnostics): raw tcgen05 accumulators of every ordered pair with the thresholds thr_d2
+// folded in, the folded bounds V, and the operand images row by row (n x kp each)
+void tc_filter_audit(Workspace& ws, const float* x, int n, int d, const float* thr_d2, int precision, float* acc,
+                     float* V, float* arows, float* brows, cudaStream_t s);
+
 // ---------------------------------------------------------------- density / detection
 // Sequential-order double mean of the first k ranks (rank stride n) -- bit-identical to the
 // host loop fastdecbase.cpp:257-274. Result left in *mean_dev.

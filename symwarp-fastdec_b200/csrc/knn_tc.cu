@@ -876,6 +876,117 @@ __global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, i
     }
 }
 
+// ------------------------------------------------------------------ filter audit (diagnostics)
+// Folds a given threshold into every row of the A image exactly as the list merge does (filter_bound
+// of the exact fp32 norm, fold_bound with the TF32 norm) and records the folded bound V.
+__global__ void audit_fold_kernel(const float* __restrict__ thr_d2, const float* __restrict__ norms,
+                                  const float* __restrict__ ntf, int n, int d, int kp, int exact,
+                                  unsigned char* __restrict__ aimg, float* __restrict__ V_out)
+{
+    const int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= n) return;
+    float V, w;
+    fold_bound(filter_bound(thr_d2[p], norms[p], d, kp, exact), ntf[p], kp, exact, V, w);
+    store_fold(aimg, p, d, kp, w);
+    V_out[p] = V;
+}
+
+// One tile per CTA (128 threads): row block X against the column pair (Y, Y + 1) with the same
+// operand images, descriptors and tcgen05.mma kind::tf32 instructions as knn_tile_tc, then every
+// accumulator word to acc_out[i * n + j]. Single stage, every wait bounded; on a timeout the CTA
+// records an error, waits (bounded) for what it issued, frees its TMEM and returns.
+__global__ void __launch_bounds__(128, 1) audit_tile_kernel(const unsigned char* __restrict__ aimg,
+                                                           const unsigned char* __restrict__ bimg, int n, int kp,
+                                                           int T, float* __restrict__ acc_out, int* err)
+{
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* sm = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    __shared__ __align__(8) uint64_t bar[2];
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int abort_flag;
+    const int panels = kp / 8;
+    const int X = blockIdx.x, Y = 2 * blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    unsigned char* cols = sm;                                   // panel p: block Y then Y + 1 (8 KB)
+    unsigned char* rows = sm + (size_t)panels * kCols * 32;     // panel p: block X (4 KB)
+    const uint32_t blk_bytes = (uint32_t)panels * kRows * 32;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_slot)),
+                     "r"(256)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    bool issued = false;
+    if (threadIdx.x == 0) {
+        const unsigned char* y0 = bimg + (size_t)Y * blk_bytes;
+        const unsigned char* y1 = bimg + (size_t)(Y + 1) * blk_bytes;   // block T is the poison block
+        mbar_expect_tx(&bar[0], 3 * blk_bytes);
+        bulk_load(rows, aimg + (size_t)X * blk_bytes, blk_bytes, &bar[0]);
+        for (int p = 0; p < panels; ++p) {
+            bulk_load(cols + p * kCols * 32, y0 + p * kRows * 32, kRows * 32, &bar[0]);
+            bulk_load(cols + p * kCols * 32 + kRows * 32, y1 + p * kRows * 32, kRows * 32, &bar[0]);
+        }
+        if (mbar_wait(&bar[0], 0, &abort_flag, err, 11)) {
+            tc_fence_after();
+            const uint64_t ad = sw32_desc(su32(rows)), cd = sw32_desc(su32(cols));
+            for (int p = 0; p < panels; ++p)
+                mma_tf32(tmem, ad + (uint64_t)(p * ((kRows * 32) >> 4)), cd + (uint64_t)(p * ((kCols * 32) >> 4)),
+                         p > 0 ? 1u : 0u);
+            mma_commit(&bar[1]);
+            issued = true;
+        } else {
+            // the copies may still be in flight: give them the same bounded time before leaving
+            const long long t0 = clock64();
+            while (!mbar_try_wait(&bar[0], 0) && clock64() - t0 < kWaitCycles) {
+            }
+        }
+    }
+    __syncwarp();
+    if (mbar_wait(&bar[1], 0, &abort_flag, err, 12)) {
+        tc_fence_after();
+        const int row = X * kRows + warp * 32 + lane;
+        for (int c = 0; c < kCols; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, r);
+            tmem_wait(r);
+            const int j0 = Y * kRows + c;
+            if (row < n)
+#pragma unroll
+                for (int q = 0; q < 32; ++q)
+                    if (j0 + q < n) acc_out[(size_t)row * n + j0 + q] = __uint_as_float(r[q]);
+        }
+    } else if (threadIdx.x == 0 && issued) {
+        // an MMA was issued but its completion never showed: wait (bounded) before freeing TMEM
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&bar[1], 0) && clock64() - t0 < kWaitCycles) {
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256) : "memory");
+}
+
+// the operand image row i (K entries) in natural order
+__global__ void audit_unswizzle_kernel(const unsigned char* __restrict__ img, int n, int kp, float* __restrict__ out)
+{
+    const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (size_t)n * kp) return;
+    const int i = (int)(t / kp), k = (int)(t % kp);
+    out[t] = *reinterpret_cast<const float*>(img + image_offset(i, k, kp));
+}
+
 }  // namespace tc
 
 // ------------------------------------------------------------------ host side
@@ -1051,6 +1162,41 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     if (a.ng > 1) tc::knn_tile_tc<true><<<grid, tc::kThreads, smem, s>>>(a);
     else tc::knn_tile_tc<false><<<grid, tc::kThreads, smem, s>>>(a);
     FDB_LAUNCHED();
+}
+
+// Filter audit (diagnostics, small n): the raw tcgen05 accumulators acc'(i, j) for every ordered pair
+// with thresholds thr_d2 folded in as the list merge folds them, the folded bounds V, and the A / B
+// operand images row by row, so a test can compare the tensor cores' FP32 accumulation with the exact
+// sum of the same TF32 operands and check the filter's margin.
+void tc_filter_audit(Workspace& ws, const float* x, int n, int d, const float* thr_d2, int precision, float* acc,
+                     float* V, float* arows, float* brows, cudaStream_t s)
+{
+    FDB_REQUIRE(tc_engine_supported(d), "the tcgen05 engine does not support this dimension/device");
+    const int T = (n + kBlock - 1) / kBlock;
+    float* norms = ws.norms.as<float>((size_t)T * kBlock + kBlock);
+    float* U = ws.fthr.as<float>((size_t)T * kBlock + kBlock);
+    compute_norms(x, n, n, d, norms, s);
+    const TcFold fold = tc_prepare(ws, x, n, n, d, norms, U, nullptr, s);
+    TcState& st = state_of_current_device();
+    const int kp = st.kp;
+    tc::audit_fold_kernel<<<(n + 127) / 128, 128, 0, s>>>(thr_d2, norms, fold.ntf, n, d, kp,
+                                                          precision == FDB200_FP32 ? 1 : 0, fold.aimg, V);
+    FDB_LAUNCHED();
+    int* err = ws.flags.as<int>(16);
+    FDB_CUDA(cudaMemsetAsync(err, 0, sizeof(int) * 16, s));
+    const size_t smem = (size_t)(kp / 8) * (tc::kCols + tc::kRows) * 32 + 1024;
+    FDB_REQUIRE(smem <= 227 * 1024, "filter audit: K too large for one stage");
+    FDB_CUDA(cudaFuncSetAttribute(tc::audit_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    tc::audit_tile_kernel<<<dim3(T, (T + 1) / 2), 128, smem, s>>>(st.A, st.B, n, kp, T, acc, err);
+    FDB_LAUNCHED();
+    const size_t cnt = (size_t)n * kp;
+    tc::audit_unswizzle_kernel<<<(unsigned)((cnt + 255) / 256), 256, 0, s>>>(st.A, n, kp, arows);
+    FDB_LAUNCHED();
+    tc::audit_unswizzle_kernel<<<(unsigned)((cnt + 255) / 256), 256, 0, s>>>(st.B, n, kp, brows);
+    FDB_LAUNCHED();
+    FDB_CUDA(cudaMemcpyAsync(ws.pinned, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    FDB_CUDA(cudaStreamSynchronize(s));
+    if (ws.pinned[0]) throw Error(FDB200_EINTERNAL, "filter audit kernel stopped on a bounded wait");
 }
 
 }  // namespace fdb

@@ -67,7 +67,7 @@ EXPORTS = ["fdb200_opts_init", "fdb200_last_error", "fdb200_abi_version", "fdb20
            "fdb200_release", "fdb200_density_noalloc", "fdb200_csv_shape", "fdb200_read_csv",
            "fdb200_write_csv", "fdb200_fbin_shape", "fdb200_read_fbin", "fdb200_write_fbin", "fdb200_knn_graph_save",
            "fdb200_knn_graph_shape", "fdb200_knn_graph_load", "fdb200_density_detection", "fdb200_dc_stage",
-           "fdb200_dc_select"]
+           "fdb200_dc_select", "fdb200_debug_tc_filter"]
 
 _lib = None
 
@@ -113,6 +113,7 @@ def lib():
         L.fdb200_density_detection.argtypes = [vp, vp, i, i, i, op, vp, vp, vp, ipp, ipp]
         L.fdb200_dc_stage.argtypes = [i, vp, i, i, vp, vp, i, i, i, op, vp, vp]
         L.fdb200_dc_select.argtypes = [vp, vp, i, vp, vp, i, op, vp, vp]
+        L.fdb200_debug_tc_filter.argtypes = [vp, i, i, vp, op, vp, vp, vp, vp, ipp]
         _lib = L
     return _lib
 
@@ -376,6 +377,27 @@ def final_cluster_device(parent, centers, labels, stream=None, device=0):
     o = make_opts(on_device=True, stream=stream, device=device)
     _check(lib().fdb200_final_cluster(_ptr(parent), parent.shape[0], _ptr(centers), centers.shape[0],
                                       ctypes.byref(o), _ptr(labels)))
+
+
+def debug_tc_filter(x_dm, thr_d2, precision="fp32"):
+    """Diagnostics (fdb200_debug_tc_filter): the raw tcgen05 filter accumulators for every ordered pair
+    of a small dim-major float32 dataset with per-point thresholds (squared distances) folded in.
+    Returns (acc (n, n), V (n,), A rows (n, K), B rows (n, K)) as numpy arrays."""
+    import torch
+    x = torch.from_numpy(_f32(x_dm)).cuda()
+    d, n = x.shape
+    thr = torch.from_numpy(_f32(thr_d2)).cuda()
+    kp = ((d + 6 + 7) // 8) * 8
+    acc = torch.empty((n, n), dtype=torch.float32, device=x.device)
+    V = torch.empty(n, dtype=torch.float32, device=x.device)
+    ar = torch.empty((n, kp), dtype=torch.float32, device=x.device)
+    br = torch.empty((n, kp), dtype=torch.float32, device=x.device)
+    kpo = ctypes.c_int(0)
+    o = make_opts(on_device=True, precision=precision, device=x.device.index or 0)
+    _check(lib().fdb200_debug_tc_filter(_ptr(x), n, d, _ptr(thr), ctypes.byref(o), _ptr(acc), _ptr(V), _ptr(ar),
+                                        _ptr(br), ctypes.byref(kpo)))
+    assert kpo.value == kp
+    return acc.cpu().numpy(), V.cpu().numpy(), ar.cpu().numpy(), br.cpu().numpy()
 
 
 def release(device=0):
