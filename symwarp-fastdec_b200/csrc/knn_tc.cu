@@ -1184,7 +1184,8 @@ void tc_filter_audit(Workspace& ws, const float* x, int n, int d, const float* t
     FDB_LAUNCHED();
     int* err = ws.flags.as<int>(16);
     FDB_CUDA(cudaMemsetAsync(err, 0, sizeof(int) * 16, s));
-    const size_t smem = (size_t)(kp / 8) * (tc::kCols + tc::kRows) * 32 + 1024;
+    // at least 120 KB, so that one CTA (and one TMEM allocation) runs per SM
+    const size_t smem = std::max<size_t>((size_t)(kp / 8) * (tc::kCols + tc::kRows) * 32 + 1024, 120 * 1024);
     FDB_REQUIRE(smem <= 227 * 1024, "filter audit: K too large for one stage");
     FDB_CUDA(cudaFuncSetAttribute(tc::audit_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     tc::audit_tile_kernel<<<dim3(T, (T + 1) / 2), 128, smem, s>>>(st.A, st.B, n, kp, T, acc, err);
