@@ -564,10 +564,19 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
             for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
                 int rho, Y, p_lo;
                 const int nu = item_span(a, item, rho, Y, p_lo);
+                // the issuer needs only how many of the item's pairs are tiles of this shard (all of them
+                // unsharded); the per-tile loop below then carries no schedule arithmetic, which would sit
+                // on the accumulator hand-off's critical path
+                int nt = nu;
+                if (a.nb != a.T) {
+                    nt = 0;
+                    for (int u = 0; u < nu; ++u) {
+                        Tile t;
+                        nt += tile_of(a, rho, Y, p_lo + u, t) ? 1 : 0;
+                    }
+                }
                 bool have = false;
-                for (int u = 0; u < nu; ++u) {
-                    Tile t;
-                    if (!tile_of(a, rho, Y, p_lo + u, t)) continue;
+                for (int u = 0; u < nt; ++u) {
                     if (!have) {
                         if (!mbar_wait_fast(c_full, ti & 1, abort_flag, a.err, 3)) { ok = false; break; }
                         have = true;
