@@ -121,10 +121,12 @@ bool tc_engine_supported(int d);
 struct TcFold {
     unsigned char* aimg = nullptr;
     const float* ntf = nullptr;
+    int sym = 0;   // 1: symmetric schedule (unfolded rows, strict bounds in U)
 };
-// builds the tcgen05 operand images (pre-swizzled augmented rows) and the exact point-major copy
+// builds the tcgen05 operand images (pre-swizzled augmented rows) and the exact point-major copy;
+// sym selects the symmetric schedule's unfolded row image
 TcFold tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const float* norms, const float* U,
-                  const uint64_t* thr, cudaStream_t s);
+                  const uint64_t* thr, int sym, cudaStream_t s);
 
 // filter audit (diagnostics): raw tcgen05 accumulators of every ordered pair with the thresholds thr_d2
 // folded in, the folded bounds V, and the operand images row by row (n x kp each)

@@ -186,15 +186,31 @@ __host__ __device__ inline int next_pow2(int v)
     return m;
 }
 
+// The tcgen05 filter bound of point p after a merge left its list threshold at key t: with the
+// symmetric schedule (symb) the strict unfolded bound, else with a row image the folded bound and
+// the row's w parts; the SIMT engine alone needs neither.
+__device__ __forceinline__ void update_bound(uint64_t t, int p, float* U, const float* norms, int d, int kp,
+                                             int exact, unsigned char* aimg, const float* ntf, int symb)
+{
+    const float T = (t == kEmptyKey) ? __int_as_float(0x7f800000) : __uint_as_float((uint32_t)(t >> 32));
+    if (symb) {
+        U[p] = strict_bound(filter_bound(T, norms[p], d, kp, exact));
+    } else if (aimg) {
+        float V, w;
+        fold_bound(filter_bound(T, norms[p], d, kp, exact), ntf[p], kp, exact, V, w);
+        U[p] = V;
+        store_fold(aimg, p, d, kp, w);
+    }
+}
+
 // one warp per point: list <- k-smallest of (list, new candidates); threshold <- list[k-1];
-// with the tcgen05 engine also the filter bound: U <- V and the A operand row's w parts
-// (fold_bound of the threshold plus the TF32 margin)
+// with the tcgen05 engine also the filter bound (update_bound)
 __global__ void knn_merge_kernel(uint64_t* __restrict__ lists, uint64_t* __restrict__ thr,
                                  float* __restrict__ U, const float* __restrict__ norms,
                                  const uint64_t* __restrict__ cand, int* __restrict__ cnt, int p0, int n,
                                  int k, int cap, int pw, int d, int kp, int exact,
                                  unsigned long long* __restrict__ admitted, unsigned char* __restrict__ aimg,
-                                 const float* __restrict__ ntf, const int* __restrict__ stop)
+                                 const float* __restrict__ ntf, int symb, const int* __restrict__ stop)
 {
     extern __shared__ uint64_t msm[];
     if (stop[0] | stop[1]) return;   // the round overflowed or an earlier one stopped: lists stay as they are
@@ -218,13 +234,7 @@ __global__ void knn_merge_kernel(uint64_t* __restrict__ lists, uint64_t* __restr
         const uint64_t t = buf[k - 1];
         thr[p] = t;
         cnt[p] = 0;
-        const float T = (t == kEmptyKey) ? __int_as_float(0x7f800000) : __uint_as_float((uint32_t)(t >> 32));
-        if (aimg) {
-            float V, w;
-            fold_bound(filter_bound(T, norms[p], d, kp, exact), ntf[p], kp, exact, V, w);
-            U[p] = V;
-            store_fold(aimg, p, d, kp, w);
-        }
+        update_bound(t, p, U, norms, d, kp, exact, aimg, ntf, symb);
         atomicAdd(admitted, (unsigned long long)c);
     }
 }
@@ -316,7 +326,7 @@ __global__ void __launch_bounds__(kSortedMergeWarps * 32, 4)
                             const float* __restrict__ norms, const uint64_t* __restrict__ cand,
                             int* __restrict__ cnt, int p0, int n, int k, int cap, int d, int kp, int exact,
                             unsigned long long* __restrict__ admitted, unsigned char* __restrict__ aimg,
-                            const float* __restrict__ ntf, const int* __restrict__ stop)
+                            const float* __restrict__ ntf, int symb, const int* __restrict__ stop)
 {
     __shared__ uint64_t sl_all[kSortedMergeWarps][kSortedMergeMaxK];
     __shared__ uint64_t sc_all[kSortedMergeWarps][512];
@@ -340,13 +350,7 @@ __global__ void __launch_bounds__(kSortedMergeWarps * 32, 4)
         const uint64_t t = lists[(size_t)p * k + k - 1];
         thr[p] = t;
         cnt[p] = 0;
-        const float T = (t == kEmptyKey) ? __int_as_float(0x7f800000) : __uint_as_float((uint32_t)(t >> 32));
-        if (aimg) {
-            float V, wv;
-            fold_bound(filter_bound(T, norms[p], d, kp, exact), ntf[p], kp, exact, V, wv);
-            U[p] = V;
-            store_fold(aimg, p, d, kp, wv);
-        }
+        update_bound(t, p, U, norms, d, kp, exact, aimg, ntf, symb);
         atomicAdd(admitted, (unsigned long long)c);
     }
 }
@@ -544,8 +548,12 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     res.engine_used = engine;
     const int kp = tc_kp(d);
     const int exact = cfg.precision == FDB200_FP32 ? 1 : 0;
+    // An unsharded tcgen05 call evaluates each unordered block pair once and tests both endpoints
+    // (the symmetric schedule); a shard keeps ordered pairs over its own rows, so that its lists are
+    // final without an exchange.
+    const int tc_sym = (engine == FDB200_ENGINE_TCGEN05 && nb == T) ? 1 : 0;
     TcFold fold;
-    if (engine == FDB200_ENGINE_TCGEN05) fold = tc_prepare(ws, x, cfg.ldx, n, d, norms, U, thr, s);
+    if (engine == FDB200_ENGINE_TCGEN05) fold = tc_prepare(ws, x, cfg.ldx, n, d, norms, U, thr, tc_sym, s);
 
     int mwarps;
     size_t msmem;
@@ -554,7 +562,7 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
 
     TileRound r{};
     r.x = x; r.ldx = cfg.ldx; r.n = n; r.d = d; r.norms = norms; r.thr = thr; r.U = U; r.cand = cand;
-    r.cnt = cnt; r.cap = cap; r.ovf = ovf; r.T = T; r.b_lo = b_lo; r.nb = nb;
+    r.cnt = cnt; r.cap = cap; r.ovf = ovf; r.T = T; r.b_lo = b_lo; r.nb = nb; r.sym = tc_sym;
 
     // Rounds are queued back to back with no host check in between: the schedule below depends only on
     // host state, each tile kernel tags an overflow with its round, and every later kernel of the batch
@@ -623,17 +631,17 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
             launch_tile_round(r, pl.units, pl.engine, cfg.precision, s);
             FDB_CUDA(cudaEventRecord(ev.get(2 * slot + 1), s));
             if (trace) FDB_CUDA(cudaEventRecord(m0, s));
-            // a tcgen05 or rows-only round appends only to this shard's rows; a symmetric SIMT round to
-            // any point
+            // a sharded tcgen05 round or a rows-only round appends only to this shard's rows; a symmetric
+            // round (SIMT, or tcgen05 over the whole triangle) to any point
             const bool own_rows = pl.engine == FDB200_ENGINE_TCGEN05 || pl.rows_only;
             const int plo = own_rows ? b_lo * kBlock : 0;
             const int phi = own_rows ? std::min(n, b_hi * kBlock) : n;
             if (k <= kSortedMergeMaxK && cap <= 512)
                 knn_merge_sorted_kernel<<<(phi - plo + kSortedMergeWarps - 1) / kSortedMergeWarps, kSortedMergeWarps * 32, 0, s>>>(
-                    lists, thr, U, norms, cand, cnt, plo, phi, k, cap, d, kp, exact, admitted, fold.aimg, fold.ntf, ovf);
+                    lists, thr, U, norms, cand, cnt, plo, phi, k, cap, d, kp, exact, admitted, fold.aimg, fold.ntf, fold.sym, ovf);
             else
                 knn_merge_kernel<<<(phi - plo + mwarps - 1) / mwarps, mwarps * 32, msmem, s>>>(
-                    lists, thr, U, norms, cand, cnt, plo, phi, k, cap, pw, d, kp, exact, admitted, fold.aimg, fold.ntf, ovf);
+                    lists, thr, U, norms, cand, cnt, plo, phi, k, cap, pw, d, kp, exact, admitted, fold.aimg, fold.ntf, fold.sym, ovf);
             FDB_LAUNCHED();
             if (trace) FDB_CUDA(cudaEventRecord(m1, s));
             if (!diag_done) {

@@ -36,6 +36,8 @@ struct TileRound {
                              // without updating other shards' points); 0 = symmetric units
     int delta0;              // first block offset of the round
     int ndelta;              // block offsets in the round
+    int sym;                 // tcgen05 engine: 1 = each unordered block pair once, both sides tested
+                             // (unfolded operands, U strict); 0 = ordered pairs, rows only (folded)
     unsigned long long* counters;   // optional tcgen05 diagnostics (FDB200_TRACE=1), else null
 };
 
@@ -153,6 +155,18 @@ __device__ __forceinline__ void fold_bound(float U, float nt, int kp, int exact,
     V = __fadd_ru(U, __fmul_ru(c_acc, __fadd_ru(nt, U)));
     V = __fadd_ru(V, 0x1p-100f);
     w = __fsub_rd(nt, V);
+}
+
+// The symmetric schedule leaves the operands unfolded, so acc(i, j) = |x~_i - x~_j|^2 up to FP32
+// accumulation, and tests each unordered pair for both endpoints at once: the pair survives iff
+// acc < max(U_i, U_j), with U the filter bound made strict (its next float up, so that acc <= bound
+// is acc < U). One rounded subtraction acc - max(U_i, U_j) has the sign of the exact difference
+// (a negative difference never rounds to +0), so the sign bit is the survivor bit as in the folded
+// form. Infinite bounds stay infinite (everything survives).
+__device__ __forceinline__ float strict_bound(float U)
+{
+    if (!(U < __int_as_float(0x7f800000))) return __int_as_float(0x7f800000);
+    return __uint_as_float(__float_as_uint(U) + 1u);   // U >= 0
 }
 
 // writes w's three TF32 parts into row i of the A operand image (columns d + 3 .. d + 5)

@@ -21,13 +21,17 @@
 //      test. Precision TF32 folds the plain threshold (no margin), so near-threshold candidates may
 //      be missed; the distances it does admit are still exact.
 //
-// Schedule: the engine visits ORDERED block pairs and tests rows only. A round with offsets
-// [a, a + L) covers, for every row block X, the column blocks X + delta and X - delta (mod T) for
-// each delta in the range (T/2 once when T is even), i.e. exactly the candidates the symmetric SIMT
-// round offers every point. A tile is one row block X against two adjacent column blocks
-// (Y, Y + 1) = (X + delta, X + delta + 1); a work item keeps (Y, Y + 1) resident in shared memory
-// and streams the row blocks X = Y - delta, so per 32768 pairs only one row block (28 KB at
-// d = 50) moves. A shard of the row blocks walks only the column blocks its rows reach.
+// Schedules. A tile is one row block X against two adjacent column blocks (Y, Y + 1) =
+// (X + delta, X + delta + 1); a work item keeps (Y, Y + 1) resident in shared memory and streams the
+// row blocks X = Y - delta, so per 32768 pairs only one row block (28 KB at d = 50) moves.
+//   symmetric (a call over the whole triangle): a round with offsets [a, a + L) visits the forward
+//      offsets only, so every unordered block pair is multiplied once (the offset T/2 of an even
+//      block count once, from X < T/2). The operands stay unfolded and the filter tests both
+//      endpoints: z = acc - max(U_i, U_j) < 0 (strict_bound in knn_common.cuh). A survivor is
+//      refined once and offered to both lists.
+//   ordered (a shard of the row blocks): every row block X meets the column blocks X + delta and
+//      X - delta (mod T), rows only, with the row's bound folded into A as above; a shard's lists
+//      are then final without an exchange. A shard walks only the column blocks its rows reach.
 //
 // Kernel shape (persistent, one CTA per SM, 16 warps):
 //   warp 0       producer: cp.async.bulk copies of the resident column pair (pre-swizzled 4 KB K
@@ -37,9 +41,9 @@
 //   warp 1       TMEM owner and MMA issuer (one thread): K/8 tcgen05.mma kind::tf32 per tile into
 //                one of two 256-column TMEM accumulators; tcgen05.commit frees each row stage and
 //                publishes the accumulator
-//   warps 2..9   filter: tcgen05.ld 32 columns at a time (two loads in flight), sign-bit test; a
-//                row with survivors parks its 32 accumulator words in shared memory and queues
-//                itself; then the accumulator is released
+//   warps 2..9   filter: tcgen05.ld 32 columns at a time (two loads in flight), sign-bit test (of
+//                acc' folded, of acc - max(U_i, U_j) symmetric); a row with survivors parks its 32
+//                tested words in shared memory and queues itself; then the accumulator is released
 //   warps 10..15 refine: warp r owns the tiles g = r mod 6 and drains their queues (survivor masks
 //                from the parked words, exact refine from global memory, admission, append), off
 //                the filter's critical path
@@ -81,11 +85,13 @@ struct Args {
     int n, d, kp, dp, T, stages, cap, exact;
     int gp, ng;                  // K panels per row stage, row stages per tile (ng * gp >= kp / 8)
     int diag;                    // 1: the diagonal round (X against X)
+    int sym;                     // 1: symmetric schedule (forward offsets only, both endpoints tested)
     int b_lo, nb;                // row blocks of this shard
     int r0[2], len[2], np[2];    // forward / backward offset ranges: first offset, length, pairs
     int ppi, nchunk0, items;     // pairs per work item, items of the forward range, all items
     int ywin;                    // column blocks per offset chunk: T, or the window a shard's rows reach
     const float* nrm;            // exact fp32 norms
+    const float* U;              // symmetric schedule: strict per-point filter bounds (-inf for padding)
     const uint64_t* thr;         // exact admission thresholds
     const float* xp;             // original coordinates, point-major, dp floats per row
     const unsigned char* aimg;   // row operand: per 128-row block, K/8 pre-swizzled 4 KB panels
@@ -241,10 +247,10 @@ __device__ __forceinline__ void tmem_wait(uint32_t (&r)[32])
 // ------------------------------------------------------------------ shared memory plan
 struct Smem {
     // offsets in bytes from the 1024-aligned base
-    uint32_t cols, rows, rstage, queue, qcount, raw, bars, misc, total;   // row stage q at rows + q * rstage
+    uint32_t cols, rows, rstage, queue, qcount, raw, ucol, bars, misc, total;   // row stage q at rows + q * rstage
 };
 
-__host__ __device__ inline Smem smem_plan(int kp, int stages, int gp, bool split)
+__host__ __device__ inline Smem smem_plan(int kp, int stages, int gp, bool split, bool sym)
 {
     const uint32_t qcap = split ? QueueShape<true>::cap : QueueShape<false>::cap;
     const uint32_t raw = split ? QueueShape<true>::raw : QueueShape<false>::raw;
@@ -263,6 +269,8 @@ __host__ __device__ inline Smem smem_plan(int kp, int stages, int gp, bool split
     o = (o + 15) & ~15u;
     s.raw = o;                         // per queue and filter warp: raw rows of 32 words
     o += (uint32_t)kQueues * kFilterWarps * raw * 128u;
+    s.ucol = o;                        // symmetric schedule: per filter warp, the bounds of its 128 columns
+    if (sym) o += kFilterWarps * 128u * 4u;
     s.bars = o;
     o += 48 * 8;
     s.misc = o;
@@ -282,14 +290,14 @@ struct StagePlan {
 // pipe a fixed overhead on top of its MMAs (measured at 1M x 128, K = 136, late rounds: 6,120 cycles
 // a tile with 2-panel stages, 4,420 with 4, 3,840 with 6; the MMAs alone take 2,176), so the plan
 // takes the fewest stages per tile that fit, with as many stages in flight as fit.
-inline StagePlan pick_plan(int kp)
+inline StagePlan pick_plan(int kp, bool sym)
 {
     const uint32_t limit = 227u * 1024u - 1024u;
     const int panels = kp / 8;
     StagePlan best;
     if (kp > kMaxKp || kp % 8) return best;
     for (int st = 4; st >= 2; --st)
-        if (smem_plan(kp, st, panels, false).total <= limit) {
+        if (smem_plan(kp, st, panels, false, sym).total <= limit) {
             best.stages = st;
             best.gp = panels;
             return best;
@@ -297,7 +305,7 @@ inline StagePlan pick_plan(int kp)
     for (int ng = 2; ng <= panels; ++ng) {
         const int gp = (panels + ng - 1) / ng;
         for (int st = kMaxStages; st >= 2; --st)
-            if (smem_plan(kp, st, gp, true).total <= limit) {
+            if (smem_plan(kp, st, gp, true, sym).total <= limit) {
                 best.stages = st;
                 best.gp = gp;
                 return best;
@@ -333,25 +341,53 @@ __device__ __forceinline__ int item_span(const Args& a, int item, int& rho, int&
 }
 
 struct Tile {
-    int X, Y, h1;   // row block, first column block, whether column block Y + 1 belongs to the round
+    int X, Y;     // row block, first column block
+    int h0, h1;   // whether column block Y (Y + 1) belongs to the round
 };
 
 // pair p of an item covers the offsets (delta, delta + 1) = r0 + 2p (+1): rows X = Y - delta;
-// false when X lies outside this shard's row blocks
+// false when X lies outside this shard's row blocks. Under the symmetric schedule an even block
+// count reaches the pair {X, X + T/2} from both of its blocks: only X < T/2 keeps it.
 __device__ __forceinline__ bool tile_of(const Args& a, int rho, int Y, int p, Tile& t)
 {
     t.Y = Y;
     if (a.diag) {
         t.X = Y;
+        t.h0 = 1;
         t.h1 = 0;
         return true;
     }
     const int off = 2 * p;
-    int X = Y - (a.r0[rho] + off);
+    const int dl = a.r0[rho] + off;
+    int X = Y - dl;
     if (X < 0) X += a.T;
     t.X = X;
+    t.h0 = 1;
     t.h1 = (off + 1 < a.len[rho]) ? 1 : 0;
-    return (unsigned)(X - a.b_lo) < (unsigned)a.nb;
+    if (a.sym && (a.T & 1) == 0 && X >= (a.T >> 1)) {
+        if (dl == (a.T >> 1)) t.h0 = 0;
+        if (dl + 1 == (a.T >> 1)) t.h1 = 0;
+    }
+    return (unsigned)(X - a.b_lo) < (unsigned)a.nb && (t.h0 | t.h1);
+}
+
+// how many of an item's nu pairs tile_of accepts: all of them unsharded, except under the symmetric
+// schedule the one pair whose first offset is T/2 when its row block is X >= T/2; a shard counts
+__device__ __forceinline__ int item_tiles(const Args& a, int rho, int Y, int p_lo, int nu)
+{
+    if (a.nb == a.T) {
+        if (!a.sym || a.diag || (a.T & 1)) return nu;
+        const int hT = a.T >> 1, off = hT - a.r0[rho];
+        if (off < 0 || (off & 1) || (off >> 1) < p_lo || (off >> 1) >= p_lo + nu) return nu;
+        const int X = Y >= hT ? Y - hT : Y + hT;
+        return X >= hT ? nu - 1 : nu;
+    }
+    int c = 0;
+    for (int u = 0; u < nu; ++u) {
+        Tile t;
+        c += tile_of(a, rho, Y, p_lo + u, t) ? 1 : 0;
+    }
+    return c;
 }
 
 // ------------------------------------------------------------------ refine and admission
@@ -396,15 +432,51 @@ __device__ __forceinline__ void settle_row(const Args& a, int gi, int gj0, unsig
     }
 }
 
+// the symmetric schedule's survivors of row gi among the 32 columns from gj0: each pair is refined
+// once and offered to both endpoints, each with its own exact admission test (d2 is symmetric: the
+// fmaf chain multiplies the same coordinate pairs and the two norms are added in either order)
+__device__ __forceinline__ void settle_pair_row(const Args& a, int gi, int gj0, unsigned m)
+{
+    const uint64_t thi = __ldg(a.thr + gi);
+    for (; m; m &= m - 1) {
+        const int gj = gj0 + __ffs(m) - 1;
+        if (gj >= a.n) continue;
+        const uint64_t thj = __ldg(a.thr + gj);
+        const float d2 = refine_global(a, gi, gj);
+        const uint64_t ki = pack_key(d2, gj), kj = pack_key(d2, gi);
+        if (ki < thi) tc_append(a, gi, ki);
+        if (kj < thj) tc_append(a, gj, kj);
+    }
+}
+
+template <bool kSym>
+__device__ __forceinline__ void settle(const Args& a, int gi, int gj0, unsigned m)
+{
+    if (kSym && !a.diag) settle_pair_row(a, gi, gj0, m);
+    else settle_row(a, gi, gj0, m);
+}
+
+// two accumulator words minus two bounds in one packed FP32 subtraction (rounded to nearest)
+__device__ __forceinline__ void sub2(uint32_t& x0, uint32_t& x1, float m0, float m1)
+{
+    asm("{\n\t.reg .b64 u, v;\n\t"
+        "mov.b64 u, {%0, %1};\n\t"
+        "mov.b64 v, {%2, %3};\n\t"
+        "sub.rn.f32x2 u, u, v;\n\t"
+        "mov.b64 {%0, %1}, u;\n\t}"
+        : "+r"(x0), "+r"(x1)
+        : "f"(m0), "f"(m1));
+}
+
 // ------------------------------------------------------------------ the kernel
 // kSplitK: row blocks arrive in several stages of gp K panels (large K); otherwise one stage holds a
 // whole row block and the producer and MMA loops keep their single-stage form
-template <bool kSplitK>
+template <bool kSplitK, bool kSym>
 __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    const Smem P = smem_plan(a.kp, a.stages, a.gp, kSplitK);
+    const Smem P = smem_plan(a.kp, a.stages, a.gp, kSplitK, kSym);
     constexpr int kQueueCap = QueueShape<kSplitK>::cap;
     constexpr int kSlots = QueueShape<kSplitK>::slots;
     constexpr int kRawPerWarp = QueueShape<kSplitK>::raw;
@@ -564,17 +636,10 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
             for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
                 int rho, Y, p_lo;
                 const int nu = item_span(a, item, rho, Y, p_lo);
-                // the issuer needs only how many of the item's pairs are tiles of this shard (all of them
-                // unsharded); the per-tile loop below then carries no schedule arithmetic, which would sit
-                // on the accumulator hand-off's critical path
-                int nt = nu;
-                if (a.nb != a.T) {
-                    nt = 0;
-                    for (int u = 0; u < nu; ++u) {
-                        Tile t;
-                        nt += tile_of(a, rho, Y, p_lo + u, t) ? 1 : 0;
-                    }
-                }
+                // the issuer needs only how many of the item's pairs are tiles; the per-tile loop below
+                // then carries no schedule arithmetic, which would sit on the accumulator hand-off's
+                // critical path
+                const int nt = item_tiles(a, rho, Y, p_lo, nu);
                 bool have = false;
                 for (int u = 0; u < nt; ++u) {
                     if (!have) {
@@ -659,21 +724,46 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
         bool ok = true;
         long long tw[2] = {0, 0};
         unsigned long long inline_entries = 0;
+        // symmetric schedule: the bounds of this warp's 128 columns (its half of the resident column
+        // pair) sit in its own shared-memory row for the whole item; the next item's are prefetched
+        // into registers while this one runs
+        const bool two_sided = kSym && !a.diag;
+        float* ucw = reinterpret_cast<float*>(sm + P.ucol) + e * 128;
+        float un[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        auto fetch_bounds = [&](int it) {
+            if (it >= a.items) return;
+            int rr, yy, pl;
+            item_span(a, it, rr, yy, pl);
+            int yh = yy + half;
+            if (yh >= a.T) yh -= a.T;
+            const float* src = a.U + (size_t)yh * kRows + lane;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) un[q] = __ldg(src + 32 * q);
+        };
+        if (two_sided) fetch_bounds(blockIdx.x);
         for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
             int rho, Y, p_lo;
             const int nu = item_span(a, item, rho, Y, p_lo);
+            if (two_sided) {
+                __syncwarp();
+#pragma unroll
+                for (int q = 0; q < 4; ++q) ucw[32 * q + lane] = un[q];
+                __syncwarp();
+                fetch_bounds(item + gridDim.x);
+            }
             for (int u = 0; u < nu; ++u) {
                 Tile t;
                 if (!tile_of(a, rho, Y, p_lo + u, t)) continue;
                 const int acc = g & 1, qi = g % kQueues;
+                const int gi = t.X * kRows + ra;
+                const bool row_real = gi < a.n;
+                const float Ui = kSym ? __ldg(a.U + gi) : 0.0f;   // issued ahead of the waits
                 const long long c0 = clock64();
                 if (!mbar_wait(&acc_full[acc], (g >> 1) & 1, abort_flag, a.err, 6)) { ok = false; break; }
                 if (!mbar_wait(&q_free[qi], ((g / kQueues) & 1) ^ 1, abort_flag, a.err, 7)) { ok = false; break; }
                 const long long c1 = clock64();
                 tw[0] += c1 - c0;
                 tc_fence_after();
-                const int gi = t.X * kRows + ra;
-                const bool row_real = gi < a.n;
                 int Yh = t.Y + half;
                 if (Yh >= a.T) Yh -= a.T;
                 int* qgi = qbase + qi * 3 * kQueueCap;
@@ -682,8 +772,25 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                 int nq_w = 0;   // entries this warp queued for the tile (warp-uniform)
                 int raw_w = 0;  // survivor rows this warp parked raw for the tile (warp-uniform)
                 uint32_t* rawq = reinterpret_cast<uint32_t*>(sm + P.raw) + qi * kFilterWarps * kRawPerWarp * 32;
-                auto process = [&](const uint32_t (&rv)[32], int c) {
-                    // a survivor has acc' < 0: OR the raw words and look at the sign bit
+                auto process = [&](uint32_t (&rv)[32], int c) {
+                    if constexpr (kSym) {
+                        // z = acc - max(U_i, U_j), two columns per packed subtraction; the diagonal
+                        // round tests rows only (its square holds both orders of every pair)
+                        if (two_sided) {
+                            const float4* u4 = reinterpret_cast<const float4*>(ucw + c * 32);
+#pragma unroll
+                            for (int v = 0; v < 8; ++v) {
+                                const float4 q = u4[v];
+                                sub2(rv[4 * v], rv[4 * v + 1], fmaxf(Ui, q.x), fmaxf(Ui, q.y));
+                                sub2(rv[4 * v + 2], rv[4 * v + 3], fmaxf(Ui, q.z), fmaxf(Ui, q.w));
+                            }
+                        } else {
+#pragma unroll
+                            for (int v = 0; v < 16; ++v) sub2(rv[2 * v], rv[2 * v + 1], Ui, Ui);
+                        }
+                    }
+                    // a survivor has a negative word (acc' of the folded form, z of the symmetric
+                    // one): OR the words and look at the sign bit
                     uint32_t o8[8];
 #pragma unroll
                     for (int w = 0; w < 8; ++w) o8[w] = (rv[4 * w] | rv[4 * w + 1]) | (rv[4 * w + 2] | rv[4 * w + 3]);
@@ -720,7 +827,7 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                                 qm[at] = m;
                             } else {
                                 // share full (dense early rounds): refine in place
-                                settle_row(a, gi, gj0, m);
+                                settle<kSym>(a, gi, gj0, m);
                                 ++inline_entries;
                             }
                         }
@@ -728,7 +835,7 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                     raw_w += __popc(hb);
                     nq_w += __popc(hb);
                 };
-                if (half == 0 || t.h1) {
+                if (half == 0 ? t.h0 : t.h1) {
                     // two chunks in flight: the TMEM load of chunk c + 1 overlaps the test of chunk c
                     const uint32_t tbase =
                         tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * kCols + half * 128);
@@ -812,7 +919,7 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                                  ((u.w >> 31) << (4 * v + 3));
                         }
                     }
-                    settle_row(a, qgi[ei], gq & ~31, m);
+                    settle<kSym>(a, qgi[ei], gq & ~31, m);
                 }
                 __syncwarp();
                 tw[1] += clock64() - c1;
@@ -844,9 +951,10 @@ __device__ __forceinline__ float rna_tf32(float x)
 // One thread per row: TF32-rounded row (A) and column (B) operand images, the TF32 norm, the
 // original coordinates point-major (zero padded to dp), and poison for padding rows: a padding
 // row's A entry d + 3 and a padding column's B entry d hold 2^100, far above every finite bound.
-// Rows start with the fold of an infinite bound (everything survives until the first merge).
+// Folded rows start with the fold of an infinite bound (everything survives until the first merge);
+// the symmetric schedule's rows (sym) carry the TF32 norm itself, like the columns.
 __global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, int d, int kp, int dp,
-                                  int rows_a, int rows_b, unsigned char* __restrict__ A,
+                                  int rows_a, int rows_b, int sym, unsigned char* __restrict__ A,
                                   unsigned char* __restrict__ Bm, float* __restrict__ xp, float* __restrict__ ntf)
 {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -876,7 +984,7 @@ __global__ void build_rows_kernel(const float* __restrict__ x, int ldx, int n, i
     ntf[i] = nt;
     float h, m, l;
     split3(nt, h, m, l);
-    const float av[6] = {1.0f, 1.0f, 1.0f, kFoldAll, 0.0f, 0.0f};
+    const float av[6] = {1.0f, 1.0f, 1.0f, sym ? h : kFoldAll, sym ? m : 0.0f, sym ? l : 0.0f};
     const float bv[6] = {h, m, l, 1.0f, 1.0f, 1.0f};
     for (int k = d; k < kp; ++k) {
         const int o = k - d;
@@ -1005,8 +1113,10 @@ struct TcState {
     int n = 0, d = 0, kp = 0, dp = 0, npad = 0, sms = 0, stages = 0, gp = 0;
     unsigned char *A = nullptr, *B = nullptr;
     float *xp = nullptr, *ntf = nullptr;
-    float* nrm = nullptr;   // nrm / thr belong to the scheduler
+    float* nrm = nullptr;   // nrm / thr / U belong to the scheduler
     uint64_t* thr = nullptr;
+    const float* U = nullptr;
+    int sym = 0;            // the images were built for the symmetric schedule
 };
 
 // The prepared operands of the current kNN call, one slot per device: calls on one device are
@@ -1041,14 +1151,14 @@ bool tc_engine_supported(int d)
         if (dev < 64) cc[dev].store(v);
     }
     const int kp = tc_kp(d);
-    return v == 100 && tc::pick_plan(kp).stages > 0;
+    return v == 100 && tc::pick_plan(kp, false).stages > 0 && tc::pick_plan(kp, true).stages > 0;
 }
 
 // Prepares the TF32 operand images, the TF32 norms and the point-major original coordinates for
 // one kNN call; the per-point bounds, norms and thresholds (Npad + 128 entries each) belong to the
 // scheduler, which refreshes the folded bounds in the row image after every merge.
 TcFold tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const float* norms, const float* U,
-                  const uint64_t* thr, cudaStream_t s)
+                  const uint64_t* thr, int sym, cudaStream_t s)
 {
     TcState& st = state_of_current_device();
     const int kp = tc_kp(d);
@@ -1067,8 +1177,8 @@ TcFold tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const fl
     st.xp = (float*)align((char*)st.B + b_bytes);
     st.ntf = (float*)align((char*)st.xp + x_bytes);
     // the images have no gaps: every element is written by the build kernel
-    tc::build_rows_kernel<<<(rows_b + 127) / 128, 128, 0, s>>>(x, ldx, n, d, kp, dp, npad, rows_b, st.A, st.B,
-                                                               st.xp, st.ntf);
+    tc::build_rows_kernel<<<(rows_b + 127) / 128, 128, 0, s>>>(x, ldx, n, d, kp, dp, npad, rows_b, sym, st.A,
+                                                               st.B, st.xp, st.ntf);
     FDB_LAUNCHED();
     int dev = 0;
     FDB_CUDA(cudaGetDevice(&dev));
@@ -1078,15 +1188,17 @@ TcFold tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const fl
     st.kp = kp;
     st.dp = dp;
     st.npad = npad;
-    const tc::StagePlan plan = tc::pick_plan(kp);
+    const tc::StagePlan plan = tc::pick_plan(kp, sym != 0);
     st.stages = plan.stages;
     st.gp = plan.gp;
-    (void)U;   // the folded bounds live in the row image; the scheduler keeps V for its own use
+    st.sym = sym;
+    st.U = U;   // folded bounds live in the row image; the symmetric schedule's filter reads U
     st.nrm = const_cast<float*>(norms);
     st.thr = const_cast<uint64_t*>(thr);
     TcFold f;
     f.aimg = st.A;
     f.ntf = st.ntf;
+    f.sym = sym;
     return f;
 }
 
@@ -1106,8 +1218,12 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.cap = r.cap;
     a.exact = precision == FDB200_FP32 ? 1 : 0;
     a.diag = r.diag;
+    a.sym = r.sym;
     a.b_lo = r.b_lo;
     a.nb = r.nb;
+    FDB_REQUIRE(r.sym == st.sym, "tcgen05 round and operand images disagree on the schedule");
+    FDB_REQUIRE(!r.sym || r.nb == r.T, "the symmetric tcgen05 schedule covers the whole triangle");
+    a.U = st.U;
     a.nrm = st.nrm;
     a.thr = st.thr;
     a.xp = st.xp;
@@ -1133,6 +1249,20 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     if (r.diag) {
         a.items = r.nb;
         a.ppi = 1;
+    } else if (r.sym) {
+        // forward offsets [d0, d0 + L) only: the tile of rows X and columns X + delta tests both
+        a.r0[0] = r.delta0;
+        a.len[0] = r.ndelta;
+        a.np[0] = (r.ndelta + 1) / 2;
+        a.r0[1] = a.len[1] = a.np[1] = 0;
+        const long long want_items = 8ll * st.sms;
+        const long long pairs = (long long)r.T * a.np[0];
+        int ppi = (int)std::max<long long>(1, (pairs + want_items - 1) / want_items);
+        ppi = std::min(ppi, std::max(a.np[0], 1));
+        a.ppi = ppi;
+        a.nchunk0 = (a.np[0] + ppi - 1) / ppi;
+        a.ywin = r.T;
+        a.items = r.T * a.nchunk0;
     } else {
         // forward offsets [d0, d0 + L) and their mirrors T - delta, the offset T/2 only once
         const int T = r.T, d0 = r.delta0, L = r.ndelta;
@@ -1156,20 +1286,23 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
         a.items = a.ywin * (a.nchunk0 + (a.np[1] + ppi - 1) / ppi);
     }
     if (a.items <= 0 || r.nb <= 0) return;
-    const tc::Smem P = tc::smem_plan(st.kp, st.stages, st.gp, a.ng > 1);
+    const tc::Smem P = tc::smem_plan(st.kp, st.stages, st.gp, a.ng > 1, a.sym != 0);
     const size_t smem = P.total + 1024;
     // the shared-memory opt-in is a per-device function attribute
     static std::atomic<bool> attr_set[64] = {};
     int dev = 0;
     FDB_CUDA(cudaGetDevice(&dev));
     if (dev >= 64 || !attr_set[dev].load()) {
-        FDB_CUDA(cudaFuncSetAttribute(tc::knn_tile_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        FDB_CUDA(cudaFuncSetAttribute(tc::knn_tile_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        FDB_CUDA(cudaFuncSetAttribute(tc::knn_tile_tc<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        FDB_CUDA(cudaFuncSetAttribute(tc::knn_tile_tc<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        FDB_CUDA(cudaFuncSetAttribute(tc::knn_tile_tc<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        FDB_CUDA(cudaFuncSetAttribute(tc::knn_tile_tc<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         if (dev < 64) attr_set[dev].store(true);
     }
     const int grid = std::min(a.items, st.sms);
-    if (a.ng > 1) tc::knn_tile_tc<true><<<grid, tc::kThreads, smem, s>>>(a);
-    else tc::knn_tile_tc<false><<<grid, tc::kThreads, smem, s>>>(a);
+    auto kern = a.ng > 1 ? (a.sym ? tc::knn_tile_tc<true, true> : tc::knn_tile_tc<true, false>)
+                         : (a.sym ? tc::knn_tile_tc<false, true> : tc::knn_tile_tc<false, false>);
+    kern<<<grid, tc::kThreads, smem, s>>>(a);
     FDB_LAUNCHED();
 }
 
@@ -1185,7 +1318,7 @@ void tc_filter_audit(Workspace& ws, const float* x, int n, int d, const float* t
     float* norms = ws.norms.as<float>((size_t)T * kBlock + kBlock);
     float* U = ws.fthr.as<float>((size_t)T * kBlock + kBlock);
     compute_norms(x, n, n, d, norms, s);
-    const TcFold fold = tc_prepare(ws, x, n, n, d, norms, U, nullptr, s);
+    const TcFold fold = tc_prepare(ws, x, n, n, d, norms, U, nullptr, 0, s);
     TcState& st = state_of_current_device();
     const int kp = st.kp;
     tc::audit_fold_kernel<<<(n + 127) / 128, 128, 0, s>>>(thr_d2, norms, fold.ntf, n, d, kp,
