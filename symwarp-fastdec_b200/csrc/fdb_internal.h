@@ -60,7 +60,7 @@ struct Workspace {
     cudaStream_t own_stream = nullptr;
     int* pinned = nullptr;                 // small pinned host scratch for flags / counters
     DevBuf data, norms, lists, thr, fthr, cand, cnt, flags;
-    DevBuf dist, idx, den, parent, cores, scan, mean_tmp, dc_tmp, dc_sel, labels_tmp, misc, ops, misc2;
+    DevBuf dist, idx, den, parent, cores, scan, mean_tmp, dc_tmp, dc_sel, labels_tmp, misc, ops, misc2, spill;
     void release_all();
 };
 

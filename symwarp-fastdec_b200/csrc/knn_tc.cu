@@ -103,6 +103,9 @@ struct Args {
     int* drain_err;                 // set when an abort's drain of copies / MMAs in flight ran out
     int tag;                        // the round's tag (its index in the host's batch + 1)
     int withhold_first_row_copy;    // failure injection: the first row stage is never filled
+    uint4* spill;                   // rows a filter warp could not queue: (gi, first column, mask)
+    int* spill_count;               // entries written (the post-pass refines min(count, spill_cap))
+    int spill_cap;
     unsigned long long* counters;   // optional trace counters
 };
 
@@ -471,6 +474,19 @@ __device__ __forceinline__ void sub2(uint32_t& x0, uint32_t& x1, float m0, float
 // ------------------------------------------------------------------ the kernel
 // kSplitK: row blocks arrive in several stages of gp K panels (large K); otherwise one stage holds a
 // whole row block and the producer and MMA loops keep their single-stage form
+// the spill list of one tile launch: exact refine and admission of every spilled row, after the tiles
+template <bool kSym>
+__global__ void __launch_bounds__(256) spill_settle_kernel(const __grid_constant__ Args a)
+{
+    // an overflowed or stopped round is re-planned (or abandoned): nothing to settle
+    if (*(volatile const int*)a.ovf | *(volatile const int*)a.err) return;
+    const int cnt = min(*(volatile const int*)a.spill_count, a.spill_cap);
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < cnt; t += gridDim.x * blockDim.x) {
+        const uint4 e = a.spill[t];
+        settle<kSym>(a, (int)e.x, (int)e.y, e.z);
+    }
+}
+
 template <bool kSplitK, bool kSym>
 __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
 {
@@ -826,8 +842,12 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                                 qgj[at] = gj0;
                                 qm[at] = m;
                             } else {
-                                // share full (dense early rounds): refine in place
-                                settle<kSym>(a, gi, gj0, m);
+                                // share full (dense early rounds): the row goes to the round's spill
+                                // list, which a post-pass kernel refines after the tiles; keeping the
+                                // refine out of this loop keeps the code every filter warp runs small
+                                const int at = atomicAdd(a.spill_count, 1);
+                                if (at < a.spill_cap) a.spill[at] = make_uint4((unsigned)gi, (unsigned)gj0, m, 0u);
+                                else atomicExch(a.ovf, a.tag);   // re-planned like a candidate overflow
                                 ++inline_entries;
                             }
                         }
@@ -1117,6 +1137,9 @@ struct TcState {
     uint64_t* thr = nullptr;
     const float* U = nullptr;
     int sym = 0;            // the images were built for the symmetric schedule
+    uint4* spill = nullptr; // spill list of the filter warps, its counter, its capacity
+    int* spill_count = nullptr;
+    int spill_cap = 0;
 };
 
 // The prepared operands of the current kNN call, one slot per device: calls on one device are
@@ -1176,6 +1199,12 @@ TcFold tc_prepare(Workspace& ws, const float* x, int ldx, int n, int d, const fl
     st.B = (unsigned char*)align((char*)st.A + a_bytes);
     st.xp = (float*)align((char*)st.B + b_bytes);
     st.ntf = (float*)align((char*)st.xp + x_bytes);
+    // spill list: 48 entries a point cover the densest tcgen05 round measured (43 a point at the
+    // headline shape); a round that fills it is re-planned in halves like a candidate overflow
+    st.spill_cap = (int)std::min<long long>(48ll * npad, 1ll << 28);
+    uint4* sp = ws.spill.as<uint4>((size_t)st.spill_cap + 1);
+    st.spill_count = reinterpret_cast<int*>(sp);
+    st.spill = sp + 1;
     // the images have no gaps: every element is written by the build kernel
     tc::build_rows_kernel<<<(rows_b + 127) / 128, 128, 0, s>>>(x, ldx, n, d, kp, dp, npad, rows_b, sym, st.A,
                                                                st.B, st.xp, st.ntf);
@@ -1246,6 +1275,9 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     }()};
     a.withhold_first_row_copy = (inject_left.load(std::memory_order_relaxed) && inject_left.exchange(0)) ? 1 : 0;
     a.counters = r.counters;
+    a.spill = st.spill;
+    a.spill_count = st.spill_count;
+    a.spill_cap = st.spill_cap;
     if (r.diag) {
         a.items = r.nb;
         a.ppi = 1;
@@ -1302,7 +1334,11 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     const int grid = std::min(a.items, st.sms);
     auto kern = a.ng > 1 ? (a.sym ? tc::knn_tile_tc<true, true> : tc::knn_tile_tc<true, false>)
                          : (a.sym ? tc::knn_tile_tc<false, true> : tc::knn_tile_tc<false, false>);
+    FDB_CUDA(cudaMemsetAsync(st.spill_count, 0, sizeof(int), s));
     kern<<<grid, tc::kThreads, smem, s>>>(a);
+    FDB_LAUNCHED();
+    auto post = a.sym ? tc::spill_settle_kernel<true> : tc::spill_settle_kernel<false>;
+    post<<<st.sms * 4, 256, 0, s>>>(a);
     FDB_LAUNCHED();
 }
 

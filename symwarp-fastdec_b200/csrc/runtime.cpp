@@ -52,7 +52,7 @@ void DevBuf::release()
 void Workspace::release_all()
 {
     for (DevBuf* b : {&data, &norms, &lists, &thr, &fthr, &cand, &cnt, &flags, &dist, &idx, &den,
-                      &parent, &cores, &scan, &mean_tmp, &dc_tmp, &dc_sel, &labels_tmp, &misc, &ops, &misc2})
+                      &parent, &cores, &scan, &mean_tmp, &dc_tmp, &dc_sel, &labels_tmp, &misc, &ops, &misc2, &spill})
         b->release();
 }
 
