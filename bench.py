@@ -73,6 +73,7 @@ def parse():
                    help="skip timing the reference's own GPU Fit (oracle/_ref binaries) at N=1")
     p.add_argument("--reference-gpu-runs", type=int, default=2)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-faiss-style", action="store_true", help="skip the FAISS-style GEMM + top-k kNN baseline")
     p.add_argument("--cpu-seconds", type=float, default=8.0, help="target CPU seconds per reference sample")
     a = p.parse_args()
     for key in ("n", "d", "k", "c"):
@@ -228,6 +229,54 @@ def run_reference_sample(x_full, a, target_s, steps=1, warmup=0):
                  if use_ref else "oracle CPU restatement of the whole fit"))
     return dict(value=pairs_of(ns) / mean_s, unit="pairs/s", cores=cores, kind=kind, sample=sample,
                 seconds_per_fit=mean_s, n_sample=ns)
+
+
+def run_faiss_style(x_dev, k, stream, sample=16384, batch=1024, seed=11):
+    """FAISS-style exact kNN, the comparison the reference's faissgpu backend offers (GpuIndexFlatL2,
+    faissgpu-fastdec/faissknncuda.cu:160-175): brute-force distances |q|^2 + |x|^2 - 2 q.x from one
+    cuBLAS GEMM per query batch (torch.addmm) and a k-smallest select (torch.topk, k + 1 for the point
+    itself), in FP32 and with TF32 GEMMs. A library baseline, never the product path: timed on a seeded
+    sample of queries against all n points, outside every timed region, and scaled to n queries (the
+    work per query is the same for every query). kNN only; no density, DC or labels.
+    Returns (summary, {mode: (query indices, distances, indices)}) for the sample's first batch."""
+    import torch
+    dev = x_dev.device
+    n = x_dev.shape[1]
+    X = x_dev.t().contiguous()                  # (n, d) row-major, as FAISS stores its vectors
+    nrm = (X * X).sum(1)
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    sample = min(sample, n)
+    q_all = torch.randperm(n, generator=g)[:sample].to(dev)
+
+    def one_batch(qi):
+        Q = X.index_select(0, qi)
+        dd = torch.addmm(nrm.unsqueeze(0), Q, X.t(), beta=1.0, alpha=-2.0)   # |x|^2 - 2 q.x
+        dd.add_(nrm.index_select(0, qi).unsqueeze(1)).clamp_(min=0.0)
+        return torch.topk(dd, k + 1, dim=1, largest=False)
+
+    out, first = {}, {}
+    prev = torch.backends.cuda.matmul.allow_tf32
+    try:
+        for mode, tf32 in (("fp32", False), ("tf32", True)):
+            torch.backends.cuda.matmul.allow_tf32 = tf32
+            v, i = one_batch(q_all[:batch])     # warm-up, also the returned first batch
+            first[mode] = (q_all[:batch], v, i)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for s0 in range(0, sample, batch):
+                one_batch(q_all[s0:s0 + batch])
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = e0.elapsed_time(e1)
+            out[mode] = {"sample_ms": ms, "knn_s_all_points": ms / sample * n / 1e3}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    summary = {"kind": "brute-force GEMM (cuBLAS through torch.addmm) + torch.topk, as FAISS GpuIndexFlatL2",
+               "sample_queries": sample, "batch": batch, **out,
+               "note": "kNN only, scaled from the sample to all points; a library baseline outside the timed "
+                       "region (the fit's own kNN is knn_s)"}
+    return summary, first
 
 
 def run_reference_gpu(x_host, a, centers):
@@ -397,6 +446,13 @@ def main():
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         ref = run_reference_sample(x_host, a, a.cpu_seconds)
         cpu = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    faiss_style = None
+    if rank == 0 and world == 1 and not a.no_faiss_style:
+        progress("FAISS-style baseline")
+        try:
+            faiss_style, _ = run_faiss_style(x_dev, k, stream)
+        except Exception as e:   # a baseline that fails must not take the bench line with it
+            faiss_style = {"unavailable": f"{e!r}"[:300]}
     ref_gpu = None
     if rank == 0 and world == 1 and not a.no_reference_gpu:
         progress("reference GPU fit")
@@ -441,7 +497,7 @@ def main():
            "num_cores": last.get("num_cores"), "final_k": last.get("final_k"),
            "engine_used": engine_name(stats),
            "centers": centers.cpu().tolist(), "gpu_launches": launches, "clocks": clk.summary(),
-           "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "reference_gpu": ref_gpu,
+           "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "reference_gpu": ref_gpu, "faiss_style": faiss_style,
            "vs_baseline_note": "value / (8.3353e11 pairs / 16.49 s): the reference's published symwarp FP32 "
                                "Fit on GloVe 50d, RTX A6000 (README.md:149)"}
     print(json.dumps(out), flush=True)
