@@ -68,6 +68,13 @@ constexpr int kRows = 128;               // rows per tile (one block)
 constexpr int kCols = 256;               // columns per tile (two blocks)
 constexpr int kMaxStages = 8;            // row stages in shared memory
 constexpr int kQueues = 8;               // survivor queues between filter and refine warps
+constexpr int kItemRing = 4;             // work items the producer may publish ahead of the other roles
+// Offset pairs (tiles) per work item, at most: the items in flight, claimed in order, then stream a
+// window of about 148 + 2 * 256 row blocks (19 MB at d = 50) that L2 holds, where whole-range items made
+// the 148 CTAs drift apart over the row blocks (101 GB of DRAM reads in the largest round of the
+// headline fit). Each item reloads its column pair, and the tensor pipe idles while it lands (no room
+// for a second column stage), so items are not made shorter: 64 pairs cost 5 % in that round.
+constexpr int kMaxItemPairs = 256;
 // survivor queue entries and parked raw rows per filter warp and tile. The split-K shape (large K)
 // gives half of both to row stages: its MMA takes over 2,000 cycles a tile, so the filter has slack,
 // and larger row stages mean fewer of them per tile.
@@ -106,6 +113,7 @@ struct Args {
     uint4* spill;                   // rows a filter warp could not queue: (gi, first column, mask)
     int* spill_count;               // entries written (the post-pass refines min(count, spill_cap))
     int spill_cap;
+    int* item_next;                 // the launch's next unclaimed work item (CTAs claim items in order)
     unsigned long long* counters;   // optional trace counters
 };
 
@@ -474,6 +482,30 @@ __device__ __forceinline__ void sub2(uint32_t& x0, uint32_t& x1, float m0, float
 // ------------------------------------------------------------------ the kernel
 // kSplitK: row blocks arrive in several stages of gp K panels (large K); otherwise one stage holds a
 // whole row block and the producer and MMA loops keep their single-stage form
+// The next work item of a consuming role (the MMA issuer's thread, or a whole filter / refine warp)
+// from the producer's ring: lane 0 waits, reads and releases the slot, the warp gets item and status
+// by shuffle. -1: no more items (or, with ok false, the wait gave up).
+__device__ __forceinline__ int ring_take(uint64_t* it_full, uint64_t* it_empty, volatile int* ring, int seq,
+                                         volatile int* abort_flag, int* err, bool whole_warp, bool& ok)
+{
+    const int slot = seq % kItemRing;
+    int item = -1, good = 1;
+    const int lane = threadIdx.x & 31;
+    if (!whole_warp || lane == 0) {
+        good = mbar_wait(&it_full[slot], (seq / kItemRing) & 1, abort_flag, err, 14) ? 1 : 0;
+        if (good) {
+            item = ring[slot];
+            mbar_arrive(&it_empty[slot]);
+        }
+    }
+    if (whole_warp) {
+        item = __shfl_sync(0xffffffffu, item, 0);
+        good = __shfl_sync(0xffffffffu, good, 0);
+    }
+    ok = good != 0;
+    return good ? item : -1;
+}
+
 // the spill list of one tile launch: exact refine and admission of every spilled row, after the tiles
 template <bool kSym>
 __global__ void __launch_bounds__(256) spill_settle_kernel(const __grid_constant__ Args a)
@@ -508,9 +540,12 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
     uint64_t* q_full = acc_empty + 2;                // [kQueues]
     uint64_t* q_free = q_full + kQueues;             // [kQueues]
     uint64_t* drain = q_free + kQueues;              // MMA completion before an early exit
+    uint64_t* it_full = drain + 1;                   // [kItemRing] item published by the producer
+    uint64_t* it_empty = it_full + kItemRing;        // [kItemRing] item read by every other role
     volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + P.misc);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + P.misc + 16);
     volatile int* skip_flag = reinterpret_cast<volatile int*>(sm + P.misc + 32);
+    volatile int* item_ring = reinterpret_cast<volatile int*>(sm + P.misc + 48);   // [kItemRing]
     int* qcount = reinterpret_cast<int*>(sm + P.qcount);
     int* qbase = reinterpret_cast<int*>(sm + P.queue);
 
@@ -531,6 +566,10 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
             mbar_init(&q_free[q], 1);
         }
         mbar_init(drain, 1);
+        for (int q = 0; q < kItemRing; ++q) {
+            mbar_init(&it_full[q], 1);
+            mbar_init(&it_empty[q], 1 + kFilterWarps + kRefineWarps);
+        }
         *abort_flag = 0;
         // rounds are queued without a host check in between: once an earlier round overflowed or
         // stopped, this one is discarded too and does nothing
@@ -558,7 +597,18 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
             int g = 0, ti = 0, c_issued = -1;
             bool ok = true;
             long long tw[2] = {0, 0};
-            for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
+            // Items are claimed from a launch-wide counter, so the CTAs work through them in order and
+            // the row blocks streamed at any moment (rows X = Y - delta of the items in flight) stay a
+            // window that L2 holds; each claim is published to the other roles through the ring, -1
+            // at the end.
+            for (int seq = 0; ok; ++seq) {
+                const int slot = seq % kItemRing;
+                if (!mbar_wait(&it_empty[slot], ((seq / kItemRing) & 1) ^ 1, abort_flag, a.err, 13)) { ok = false; break; }
+                int item = atomicAdd(a.item_next, 1);
+                if (item >= a.items) item = -1;
+                item_ring[slot] = item;
+                mbar_arrive(&it_full[slot]);
+                if (item < 0) break;
                 int rho, Y, p_lo;
                 const int nu = item_span(a, item, rho, Y, p_lo);
                 bool have = false;
@@ -649,7 +699,9 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
             const uint64_t cdesc = sw32_desc(su32(sm + P.cols));
             const uint64_t rdesc0 = sw32_desc(su32(sm + P.rows));
             const uint64_t rstride = (uint64_t)((a.gp * kRows * 32) >> 4);   // one row stage in descriptor units
-            for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
+            for (int seq = 0; ok; ++seq) {
+                const int item = ring_take(it_full, it_empty, item_ring, seq, abort_flag, a.err, false, ok);
+                if (item < 0) break;
                 int rho, Y, p_lo;
                 const int nu = item_span(a, item, rho, Y, p_lo);
                 // the issuer needs only how many of the item's pairs are tiles; the per-tile loop below
@@ -741,31 +793,25 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
         long long tw[2] = {0, 0};
         unsigned long long inline_entries = 0;
         // symmetric schedule: the bounds of this warp's 128 columns (its half of the resident column
-        // pair) sit in its own shared-memory row for the whole item; the next item's are prefetched
-        // into registers while this one runs
+        // pair) sit in its own shared-memory row for the whole item
         const bool two_sided = kSym && !a.diag;
         float* ucw = reinterpret_cast<float*>(sm + P.ucol) + e * 128;
-        float un[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        auto fetch_bounds = [&](int it) {
-            if (it >= a.items) return;
-            int rr, yy, pl;
-            item_span(a, it, rr, yy, pl);
-            int yh = yy + half;
-            if (yh >= a.T) yh -= a.T;
-            const float* src = a.U + (size_t)yh * kRows + lane;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) un[q] = __ldg(src + 32 * q);
-        };
-        if (two_sided) fetch_bounds(blockIdx.x);
-        for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
+        for (int seq = 0; ok; ++seq) {
+            const int item = ring_take(it_full, it_empty, item_ring, seq, abort_flag, a.err, true, ok);
+            if (item < 0) break;
             int rho, Y, p_lo;
             const int nu = item_span(a, item, rho, Y, p_lo);
             if (two_sided) {
+                int yh = Y + half;
+                if (yh >= a.T) yh -= a.T;
+                const float* src = a.U + (size_t)yh * kRows + lane;
+                float un[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) un[q] = __ldg(src + 32 * q);
                 __syncwarp();
 #pragma unroll
                 for (int q = 0; q < 4; ++q) ucw[32 * q + lane] = un[q];
                 __syncwarp();
-                fetch_bounds(item + gridDim.x);
             }
             for (int u = 0; u < nu; ++u) {
                 Tile t;
@@ -899,7 +945,9 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
         bool ok = true;
         long long tw[2] = {0, 0};
         unsigned long long entries = 0;
-        for (int item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
+        for (int seq = 0; ok; ++seq) {
+            const int item = ring_take(it_full, it_empty, item_ring, seq, abort_flag, a.err, true, ok);
+            if (item < 0) break;
             int rho, Y, p_lo;
             const int nu = item_span(a, item, rho, Y, p_lo);
             for (int u = 0; u < nu; ++u) {
@@ -1278,6 +1326,7 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.spill = st.spill;
     a.spill_count = st.spill_count;
     a.spill_cap = st.spill_cap;
+    a.item_next = st.spill_count + 1;
     if (r.diag) {
         a.items = r.nb;
         a.ppi = 1;
@@ -1290,7 +1339,7 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
         const long long want_items = 8ll * st.sms;
         const long long pairs = (long long)r.T * a.np[0];
         int ppi = (int)std::max<long long>(1, (pairs + want_items - 1) / want_items);
-        ppi = std::min(ppi, std::max(a.np[0], 1));
+        ppi = std::min(std::min(ppi, tc::kMaxItemPairs), std::max(a.np[0], 1));
         a.ppi = ppi;
         a.nchunk0 = (a.np[0] + ppi - 1) / ppi;
         a.ywin = r.T;
@@ -1305,11 +1354,11 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
         a.len[1] = L - e;
         a.np[0] = (a.len[0] + 1) / 2;
         a.np[1] = (a.len[1] + 1) / 2;
-        // about 8 items of real tiles per CTA so the tail of a round stays short
+        // about 8 items of real tiles per CTA so the tail of a round stays short, kMaxItemPairs at most
         const long long want_items = 8ll * st.sms;
         const long long pairs = (long long)r.nb * (a.np[0] + a.np[1]);
         int ppi = (int)std::max<long long>(1, (pairs + want_items - 1) / want_items);
-        ppi = std::min(ppi, std::max(a.np[0], 1));
+        ppi = std::min(std::min(ppi, tc::kMaxItemPairs), std::max(a.np[0], 1));
         a.ppi = ppi;
         a.nchunk0 = (a.np[0] + ppi - 1) / ppi;
         // a shard's rows X in [b_lo, b_lo + nb) meet, for one chunk of ppi offset pairs, the column
@@ -1334,7 +1383,7 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     const int grid = std::min(a.items, st.sms);
     auto kern = a.ng > 1 ? (a.sym ? tc::knn_tile_tc<true, true> : tc::knn_tile_tc<true, false>)
                          : (a.sym ? tc::knn_tile_tc<false, true> : tc::knn_tile_tc<false, false>);
-    FDB_CUDA(cudaMemsetAsync(st.spill_count, 0, sizeof(int), s));
+    FDB_CUDA(cudaMemsetAsync(st.spill_count, 0, 2 * sizeof(int), s));   // spill count, item counter
     kern<<<grid, tc::kThreads, smem, s>>>(a);
     FDB_LAUNCHED();
     auto post = a.sym ? tc::spill_settle_kernel<true> : tc::spill_settle_kernel<false>;
