@@ -36,9 +36,9 @@ sys.path.insert(0, str(ROOT / "symwarp-fastdec_b200"))
 PUBLISHED_A6000_FIT_S = 16.49          # README.md:149, symwarp FP32 Fit seconds on GloVe 50d (A6000)
 # DRAM traffic of the tile kernels over one fit of the default workload, from one ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum summed over the nine tile launches of a fit, four
-# knn_tile_simt and five knn_tile_tc: 348.8 GB read + 17.4 GB written). A one-pass metric set, so it
+# knn_tile_simt and five knn_tile_tc: 25.95 GB read + 12.83 GB written). A one-pass metric set, so it
 # was taken on the full workload.
-TILE_DRAM_BYTES_PER_FIT = 366.15e9
+TILE_DRAM_BYTES_PER_FIT = 38.78e9
 WORKLOAD = dict(n=1_291_147, d=50, k=45, c=20)
 # the synthetic configurations (fastdec_b200.datasets): the headline GloVe-like cloud, the 100k GMM and
 # the 4M x 128 scale-out mixture; --n/--d/--k/--c override a configuration's shape
