@@ -41,7 +41,7 @@
 //   warp 1       TMEM owner and MMA issuer (one thread): K/8 tcgen05.mma kind::tf32 per tile into
 //                one of two 256-column TMEM accumulators; tcgen05.commit frees each row stage and
 //                publishes the accumulator
-//   warps 2..9   filter: tcgen05.ld 32 columns at a time (two loads in flight), sign-bit test (of
+//   warps 2..9   filter: tcgen05.ld 32 columns at a time (one load in flight), sign-bit test (of
 //                acc' folded, of acc - max(U_i, U_j) symmetric); a row with survivors parks its 32
 //                tested words in shared memory and queues itself; then the accumulator is released
 //   warps 10..15 refine: warp r owns the tiles g = r mod 6 and drains their queues (survivor masks
@@ -902,22 +902,17 @@ __global__ void __launch_bounds__(kThreads, 1) knn_tile_tc(Args a)
                     nq_w += __popc(hb);
                 };
                 if (half == 0 ? t.h0 : t.h1) {
-                    // two chunks in flight: the TMEM load of chunk c + 1 overlaps the test of chunk c
+                    // one chunk at a time: a TMEM load lands within tens of cycles, and the registers
+                    // of a second buffer are worth more to the test (no spills at 120 registers)
                     const uint32_t tbase =
                         tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * kCols + half * 128);
-                    uint32_t r0[32], r1[32];
-                    tmem_ld32(tbase, r0);
-                    tmem_wait(r0);
-                    tmem_ld32(tbase + 32, r1);
-                    process(r0, 0);
-                    tmem_wait(r1);
-                    tmem_ld32(tbase + 64, r0);
-                    process(r1, 1);
-                    tmem_wait(r0);
-                    tmem_ld32(tbase + 96, r1);
-                    process(r0, 2);
-                    tmem_wait(r1);
-                    process(r1, 3);
+                    uint32_t r0[32];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        tmem_ld32(tbase + 32 * c, r0);
+                        tmem_wait(r0);
+                        process(r0, c);
+                    }
                 }
                 // the accumulator is done with: release it and hand the queue over
                 tc_fence_before();
