@@ -39,6 +39,11 @@ PUBLISHED_A6000_FIT_S = 16.49          # README.md:149, symwarp FP32 Fit seconds
 # knn_tile_simt and five knn_tile_tc: 25.95 GB read + 12.83 GB written). A one-pass metric set, so it
 # was taken on the full workload.
 TILE_DRAM_BYTES_PER_FIT = 38.78e9
+# Dense TF32 GEMM throughput of this pool's B200s, measured by `python bench.py --tf32-peak` (cuBLAS
+# 8192^3 fp32 GEMM with TF32 allowed: best of 10 launches, and back to back for 4 s with sw_power_cap
+# active at a median SM clock of 1068 MHz). MEASURED_PEAKS.json holds bf16 figures only; half of them
+# (822 / 694 TF/s) overstates TF32 on this part.
+TF32_PEAK = {"tflops": 743.5, "tflops_sustained": 602.8, "source": "measured (bench.py --tf32-peak)"}
 WORKLOAD = dict(n=1_291_147, d=50, k=45, c=20)
 # the synthetic configurations (fastdec_b200.datasets): the headline GloVe-like cloud, the 100k GMM and
 # the 4M x 128 scale-out mixture; --n/--d/--k/--c override a configuration's shape
@@ -74,6 +79,7 @@ def parse():
     p.add_argument("--reference-gpu-runs", type=int, default=2)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-faiss-style", action="store_true", help="skip the FAISS-style GEMM + top-k kNN baseline")
+    p.add_argument("--tf32-peak", action="store_true", help="measure the dense TF32 GEMM peak of GPU 0 and exit")
     p.add_argument("--cpu-seconds", type=float, default=8.0, help="target CPU seconds per reference sample")
     a = p.parse_args()
     for key in ("n", "d", "k", "c"):
@@ -184,6 +190,43 @@ def physical_gpu(local):
         if local < len(ids) and ids[local].isdigit():
             return int(ids[local])
     return local
+
+
+def measure_tf32_peak(seconds=4.0, size=8192):
+    """Dense TF32 throughput of this GPU, measured the way the bf16 figures of MEASURED_PEAKS.json are:
+    a cuBLAS GEMM (torch.matmul on fp32 operands with TF32 allowed), 2 N^3 flops, best of 10 launches
+    (burst) and launches back to back for `seconds` (sustained), CUDA events, clocks sampled meanwhile.
+    `python bench.py --tf32-peak` prints it; the figures it gave on this pool are TF32_PEAK below."""
+    import torch
+    dev = torch.device("cuda", 0)
+    torch.backends.cuda.matmul.allow_tf32 = True
+    a = torch.randn(size, size, device=dev)
+    b = torch.randn(size, size, device=dev)
+    c = torch.empty(size, size, device=dev)
+    flops = 2.0 * size ** 3
+    for _ in range(3):
+        torch.matmul(a, b, out=c)
+    torch.cuda.synchronize(dev)
+    best = float("inf")
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch.matmul(a, b, out=c)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        best = min(best, e0.elapsed_time(e1))
+    reps = max(1, int(seconds * 1e3 / best))
+    with ClockSampler(physical_gpu(0)) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            torch.matmul(a, b, out=c)
+        e1.record()
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    return {"tf32_tflops": flops / (best / 1e3) / 1e12, "tf32_tflops_sustained": flops * reps / (ms / 1e3) / 1e12,
+            "size": size, "sustained_launches": reps, "clocks": clk.summary(),
+            "gpu_name": torch.cuda.get_device_name(dev)}
 
 
 def measured_peaks():
@@ -317,6 +360,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     a.gpus = world if world > 1 else a.gpus
+
+    if a.tf32_peak:
+        print(json.dumps(measure_tf32_peak()))
+        return 0
 
     if a.impl == "reference":
         if rank != 0:
@@ -466,7 +513,7 @@ def main():
         return 0
 
     bf16, hbm, src = measured_peaks()
-    tf32_peak = bf16 / 2.0
+    tf32_peak = TF32_PEAK["tflops_sustained"]
     flops = shard_pairs * 2 * d
     achieved = flops / (tile_ms / 1e3) / 1e12 if tile_ms > 0 else None
     default_shape = vs_baseline(a, 1.0) is not None and (world, a.precision, a.engine) == (1, "fp32", "auto")
@@ -476,8 +523,9 @@ def main():
                 "frac": (achieved / tf32_peak) if achieved else None,
                 "traffic": TILE_DRAM_BYTES_PER_FIT if default_shape else None,
                 "traffic_unit": "bytes per fit (ncu, tile kernels)",
-                "peak_note": f"dense TF32 = 1/2 of the {src} sustained bf16 figure ({bf16} TF/s): the tile kernels "
-                             f"run inside the seconds-long timed loop; of {src}",
+                "peak_note": f"dense TF32, the sustained cuBLAS TF32 GEMM figure of this pool ({TF32_PEAK['tflops_sustained']} "
+                             f"TF/s, {TF32_PEAK['source']}; burst {TF32_PEAK['tflops']}): the tile kernels run inside "
+                             f"the seconds-long timed loop; of measured",
                 "launches_per_fit": rounds, "algorithmic_flops_per_fit": flops,
                 "algorithmic_note": "N(N-1)/2 pairs x 2d FLOPs (the reference's -2 X X^T GEMM work)",
                 "tensor_flops_per_fit": (float(n) * n * kp * (1 if world == 1 else 2)
