@@ -223,7 +223,8 @@ int fdb200_dc_select(const float* densities_dev, const int* cores_dev, int core_
 int fdb200_debug_tc_filter(const float* data_dev, int n, int d, const float* thr_d2_dev, const FdB200Opts* opts,
                            float* acc_dev, float* bound_dev, float* arows_dev, float* brows_dev, int* kp_out);
 
-/* Frees the library's cached device workspace on opts->device. */
+/* Frees the library's cached device workspace on opts->device. The workspace grows to what the
+ * largest call needed: for the kNN about 6 KB a point at d = 50, k = 45 (8.5 GB at 1,291,147 points). */
 int fdb200_release(const FdB200Opts* opts);
 
 /*
