@@ -50,6 +50,7 @@
 // Every mbarrier wait is bounded (about a second); on a timeout the CTA records an error code,
 // stops issuing work, frees its TMEM and returns, and the host reports the failure.
 #include "knn_common.cuh"
+#include "knn_tc_schedule.h"
 
 #include <algorithm>
 #include <atomic>
@@ -69,12 +70,6 @@ constexpr int kCols = 256;               // columns per tile (two blocks)
 constexpr int kMaxStages = 8;            // row stages in shared memory
 constexpr int kQueues = 8;               // survivor queues between filter and refine warps
 constexpr int kItemRing = 4;             // work items the producer may publish ahead of the other roles
-// Offset pairs (tiles) per work item, at most: the items in flight, claimed in order, then stream a
-// window of about 148 + 2 * 256 row blocks (19 MB at d = 50) that L2 holds, where whole-range items made
-// the 148 CTAs drift apart over the row blocks (101 GB of DRAM reads in the largest round of the
-// headline fit). Each item reloads its column pair, and the tensor pipe idles while it lands (no room
-// for a second column stage), so items are not made shorter: 64 pairs cost 5 % in that round.
-constexpr int kMaxItemPairs = 256;
 // survivor queue entries and parked raw rows per filter warp and tile. The split-K shape (large K)
 // gives half of both to row stages: its MMA takes over 2,000 cycles a tile, so the filter has slack,
 // and larger row stages mean fewer of them per tile.
@@ -88,15 +83,9 @@ constexpr int kMaxKp = 256;              // K bound; what fits in shared memory 
 constexpr long long kWaitCycles = 2000000000ll;   // ~1 s at 2 GHz
 constexpr float kPoisonNorm = 1.2676506002282294e30f;   // 2^100, exact in TF32
 
-struct Args {
-    int n, d, kp, dp, T, stages, cap, exact;
+struct Args : Sched {            // the launch's schedule (knn_tc_schedule.h) and its data
+    int n, d, kp, dp, stages, cap, exact;
     int gp, ng;                  // K panels per row stage, row stages per tile (ng * gp >= kp / 8)
-    int diag;                    // 1: the diagonal round (X against X)
-    int sym;                     // 1: symmetric schedule (forward offsets only, both endpoints tested)
-    int b_lo, nb;                // row blocks of this shard
-    int r0[2], len[2], np[2];    // forward / backward offset ranges: first offset, length, pairs
-    int ppi, nchunk0, items;     // pairs per work item, items of the forward range, all items
-    int ywin;                    // column blocks per offset chunk: T, or the window a shard's rows reach
     const float* nrm;            // exact fp32 norms
     const float* U;              // symmetric schedule: strict per-point filter bounds (-inf for padding)
     const uint64_t* thr;         // exact admission thresholds
@@ -323,82 +312,6 @@ inline StagePlan pick_plan(int kp, bool sym)
             }
     }
     return best;
-}
-
-// ------------------------------------------------------------------ schedule
-// Work item -> (offset range rho, resident column block Y, its pair indices [p_lo, p_lo + count)).
-// Every role walks the same items and tiles in the same order, so tile counters agree.
-__device__ __forceinline__ int item_span(const Args& a, int item, int& rho, int& Y, int& p_lo)
-{
-    if (a.diag) {
-        rho = 0;
-        Y = a.b_lo + item;
-        p_lo = 0;
-        return 1;
-    }
-    const int gc = item / a.ywin;
-    const int w = item - gc * a.ywin;
-    rho = gc < a.nchunk0 ? 0 : 1;
-    p_lo = (rho ? gc - a.nchunk0 : gc) * a.ppi;
-    if (a.ywin == a.T) {
-        Y = w;
-    } else {
-        // a shard: only the column blocks Y whose rows X = Y - delta (delta = r0 + 2p over the chunk)
-        // can fall in the shard's row blocks
-        Y = a.b_lo + a.r0[rho] + 2 * p_lo + w;
-        Y %= a.T;
-    }
-    return min(a.np[rho], p_lo + a.ppi) - p_lo;
-}
-
-struct Tile {
-    int X, Y;     // row block, first column block
-    int h0, h1;   // whether column block Y (Y + 1) belongs to the round
-};
-
-// pair p of an item covers the offsets (delta, delta + 1) = r0 + 2p (+1): rows X = Y - delta;
-// false when X lies outside this shard's row blocks. Under the symmetric schedule an even block
-// count reaches the pair {X, X + T/2} from both of its blocks: only X < T/2 keeps it.
-__device__ __forceinline__ bool tile_of(const Args& a, int rho, int Y, int p, Tile& t)
-{
-    t.Y = Y;
-    if (a.diag) {
-        t.X = Y;
-        t.h0 = 1;
-        t.h1 = 0;
-        return true;
-    }
-    const int off = 2 * p;
-    const int dl = a.r0[rho] + off;
-    int X = Y - dl;
-    if (X < 0) X += a.T;
-    t.X = X;
-    t.h0 = 1;
-    t.h1 = (off + 1 < a.len[rho]) ? 1 : 0;
-    if (a.sym && (a.T & 1) == 0 && X >= (a.T >> 1)) {
-        if (dl == (a.T >> 1)) t.h0 = 0;
-        if (dl + 1 == (a.T >> 1)) t.h1 = 0;
-    }
-    return (unsigned)(X - a.b_lo) < (unsigned)a.nb && (t.h0 | t.h1);
-}
-
-// how many of an item's nu pairs tile_of accepts: all of them unsharded, except under the symmetric
-// schedule the one pair whose first offset is T/2 when its row block is X >= T/2; a shard counts
-__device__ __forceinline__ int item_tiles(const Args& a, int rho, int Y, int p_lo, int nu)
-{
-    if (a.nb == a.T) {
-        if (!a.sym || a.diag || (a.T & 1)) return nu;
-        const int hT = a.T >> 1, off = hT - a.r0[rho];
-        if (off < 0 || (off & 1) || (off >> 1) < p_lo || (off >> 1) >= p_lo + nu) return nu;
-        const int X = Y >= hT ? Y - hT : Y + hT;
-        return X >= hT ? nu - 1 : nu;
-    }
-    int c = 0;
-    for (int u = 0; u < nu; ++u) {
-        Tile t;
-        c += tile_of(a, rho, Y, p_lo + u, t) ? 1 : 0;
-    }
-    return c;
 }
 
 // ------------------------------------------------------------------ refine and admission
@@ -1283,16 +1196,11 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.d = r.d;
     a.kp = st.kp;
     a.dp = st.dp;
-    a.T = r.T;
     a.stages = st.stages;
     a.gp = st.gp;
     a.ng = (st.kp / 8 + st.gp - 1) / st.gp;
     a.cap = r.cap;
     a.exact = precision == FDB200_FP32 ? 1 : 0;
-    a.diag = r.diag;
-    a.sym = r.sym;
-    a.b_lo = r.b_lo;
-    a.nb = r.nb;
     FDB_REQUIRE(r.sym == st.sym, "tcgen05 round and operand images disagree on the schedule");
     FDB_REQUIRE(!r.sym || r.nb == r.T, "the symmetric tcgen05 schedule covers the whole triangle");
     a.U = st.U;
@@ -1322,45 +1230,7 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.spill_count = st.spill_count;
     a.spill_cap = st.spill_cap;
     a.item_next = st.spill_count + 1;
-    if (r.diag) {
-        a.items = r.nb;
-        a.ppi = 1;
-    } else if (r.sym) {
-        // forward offsets [d0, d0 + L) only: the tile of rows X and columns X + delta tests both
-        a.r0[0] = r.delta0;
-        a.len[0] = r.ndelta;
-        a.np[0] = (r.ndelta + 1) / 2;
-        a.r0[1] = a.len[1] = a.np[1] = 0;
-        const long long want_items = 8ll * st.sms;
-        const long long pairs = (long long)r.T * a.np[0];
-        int ppi = (int)std::max<long long>(1, (pairs + want_items - 1) / want_items);
-        ppi = std::min(std::min(ppi, tc::kMaxItemPairs), std::max(a.np[0], 1));
-        a.ppi = ppi;
-        a.nchunk0 = (a.np[0] + ppi - 1) / ppi;
-        a.ywin = r.T;
-        a.items = r.T * a.nchunk0;
-    } else {
-        // forward offsets [d0, d0 + L) and their mirrors T - delta, the offset T/2 only once
-        const int T = r.T, d0 = r.delta0, L = r.ndelta;
-        const int e = ((T & 1) == 0 && d0 + L - 1 == T / 2) ? 1 : 0;
-        a.r0[0] = d0;
-        a.len[0] = L;
-        a.r0[1] = T - (d0 + L - 1) + e;
-        a.len[1] = L - e;
-        a.np[0] = (a.len[0] + 1) / 2;
-        a.np[1] = (a.len[1] + 1) / 2;
-        // about 8 items of real tiles per CTA so the tail of a round stays short, kMaxItemPairs at most
-        const long long want_items = 8ll * st.sms;
-        const long long pairs = (long long)r.nb * (a.np[0] + a.np[1]);
-        int ppi = (int)std::max<long long>(1, (pairs + want_items - 1) / want_items);
-        ppi = std::min(std::min(ppi, tc::kMaxItemPairs), std::max(a.np[0], 1));
-        a.ppi = ppi;
-        a.nchunk0 = (a.np[0] + ppi - 1) / ppi;
-        // a shard's rows X in [b_lo, b_lo + nb) meet, for one chunk of ppi offset pairs, the column
-        // blocks Y = X + delta: a window of nb + 2 ppi - 1 blocks (all T when unsharded)
-        a.ywin = (r.nb == T) ? T : std::min(T, r.nb + 2 * ppi - 1);
-        a.items = a.ywin * (a.nchunk0 + (a.np[1] + ppi - 1) / ppi);
-    }
+    tc::plan_schedule(a, r.T, r.diag, r.sym, r.b_lo, r.nb, r.delta0, r.ndelta, st.sms);
     if (a.items <= 0 || r.nb <= 0) return;
     const tc::Smem P = tc::smem_plan(st.kp, st.stages, st.gp, a.ng > 1, a.sym != 0);
     const size_t smem = P.total + 1024;
