@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define FDB200_ABI_VERSION 2
+#define FDB200_ABI_VERSION 3
 
 enum {
     FDB200_OK = 0,
@@ -48,6 +48,20 @@ enum { FDB200_FP32 = 0, FDB200_TF32 = 1 };              /* distance precision */
 enum { FDB200_LAPLACIAN = 0, FDB200_GAUSSIAN = 1 };    /* density kernel (USE_GAUSSIAN_KERNEL) */
 enum { FDB200_ENGINE_AUTO = 0, FDB200_ENGINE_SIMT = 1, FDB200_ENGINE_TCGEN05 = 2 };
 
+/*
+ * Round hook of a symmetric sharded kNN (fdb200_knn_partial with round_hook set). Between the rounds
+ * of the triangle the library asks the caller to combine two small device arrays over all shards,
+ * on `stream`, and returns without waiting: the caller enqueues the combination (an NCCL all-reduce,
+ * say) on that stream and returns. kind FDB200_HOOK_FLAGS: `count` int32 flags (the round's overflow
+ * tag and error code) to combine by MAX, before the round's list merge, so that every shard discards
+ * and re-plans an overflowed round alike. kind FDB200_HOOK_THRESHOLDS: `count` packed uint64 per-point
+ * thresholds (see fdb200_knn_partial) to combine by unsigned MIN after the merge: the k-th key of any
+ * shard's partial list bounds the k-th key of the union, so every shard filters with the tightest.
+ * Every shard makes the same calls in the same order. No counterpart in the reference (single-GPU).
+ */
+enum { FDB200_HOOK_FLAGS = 0, FDB200_HOOK_THRESHOLDS = 1 };
+typedef void (*fdb200_round_hook)(void* ctx, int kind, void* dev_ptr, long long count, void* stream);
+
 typedef struct FdB200Opts {
     int struct_size;          /* sizeof(FdB200Opts); set by fdb200_opts_init */
     int device;               /* CUDA device ordinal (Dataset::cuda_device_id, dataset.h:30) */
@@ -67,6 +81,12 @@ typedef struct FdB200Opts {
                                  cudaStreamLegacy to run on the legacy default stream) */
     int shard_block_lo;       /* explicit shard: the 128-point row blocks [shard_block_lo, shard_block_hi) */
     int shard_block_hi;       /* (-1, -1 = the even split given by shard_rank / shard_count) */
+    fdb200_round_hook round_hook;   /* fdb200_knn_partial: NULL = ordered shards (each shard's rows
+                                       against every column, its own lists final, no exchange);
+                                       set = symmetric shards (each unordered block pair once over all
+                                       shards, partial lists of every point, thresholds combined
+                                       through the hook between rounds) */
+    void* round_hook_ctx;     /* passed to round_hook */
 } FdB200Opts;
 
 typedef struct FdB200Stats {
@@ -158,6 +178,12 @@ int fdb200_final_cluster(const int* parent, int n, const int* centers, int c,
  * A packed entry is ((uint64)float_bits(d2) << 32) | index; lists are point-major, n * k,
  * ascending, padded with UINT64_MAX. No counterpart in the reference (it is single-GPU); the
  * merged result equals fdb200_knn's.
+ * With the tcgen05 engine and no round_hook a shard tests its own row blocks against every column
+ * (ordered pairs): the lists of its own points are then final and need no exchange. With a
+ * round_hook (see fdb200_round_hook) a shard multiplies only the block pairs whose first block is
+ * its own, once, tests both endpoints and keeps partial lists of every point, which the caller
+ * exchanges to their owners and merges (fdb200_merge_lists); the dense first rounds then run on
+ * symmetric SIMT tiles.
  */
 int fdb200_knn_partial(const float* data_dev, int n, int d, int k, const FdB200Opts* opts,
                        uint64_t* lists_dev, FdB200Stats* stats);

@@ -51,6 +51,8 @@ KnnConfig knn_config(int n, int d, int k, const FdB200Opts& o)
     c.cand_capacity = o.cand_capacity;
     c.block_lo = o.shard_block_lo;
     c.block_hi = o.shard_block_hi;
+    c.round_hook = o.round_hook;
+    c.round_hook_ctx = o.round_hook_ctx;
     return c;
 }
 

@@ -93,6 +93,8 @@ struct KnnConfig {
     int shard_rank = 0, shard_count = 1;
     int block_lo = -1, block_hi = -1;   // explicit row-block range of the shard (-1: from rank / count)
     int cand_capacity = 0;
+    fdb200_round_hook round_hook = nullptr;   // symmetric shards: thresholds combined between rounds
+    void* round_hook_ctx = nullptr;
 };
 
 struct KnnResult {

@@ -355,6 +355,17 @@ __global__ void __launch_bounds__(kSortedMergeWarps * 32, 4)
     }
 }
 
+// symmetric shards: the filter bounds from the thresholds just combined over the shards
+__global__ void refresh_bounds_kernel(const uint64_t* __restrict__ thr, const float* __restrict__ norms,
+                                      float* __restrict__ U, int n, int d, int kp, int exact)
+{
+    const int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= n) return;
+    const uint64_t t = thr[p];
+    const float T = (t == kEmptyKey) ? __int_as_float(0x7f800000) : __uint_as_float((uint32_t)(t >> 32));
+    U[p] = strict_bound(filter_bound(T, norms[p], d, kp, exact));
+}
+
 // per-point state before the first round: empty lists admit everything, padding nothing
 __global__ void init_point_state_kernel(int n, int rows, float* __restrict__ norms, uint64_t* __restrict__ thr,
                                         float* __restrict__ U)
@@ -549,9 +560,12 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     const int kp = tc_kp(d);
     const int exact = cfg.precision == FDB200_FP32 ? 1 : 0;
     // An unsharded tcgen05 call evaluates each unordered block pair once and tests both endpoints
-    // (the symmetric schedule); a shard keeps ordered pairs over its own rows, so that its lists are
-    // final without an exchange.
-    const int tc_sym = (engine == FDB200_ENGINE_TCGEN05 && nb == T) ? 1 : 0;
+    // (the symmetric schedule). A shard with a round hook does the same over the block pairs whose
+    // first block is its own, keeps partial lists of every point and has its thresholds combined
+    // with the other shards' through the hook after every round; a shard without one keeps ordered
+    // pairs over its own rows, so that its lists are final without an exchange.
+    const bool hooked = cfg.round_hook != nullptr;
+    const int tc_sym = (engine == FDB200_ENGINE_TCGEN05 && (nb == T || hooked)) ? 1 : 0;
     TcFold fold;
     if (engine == FDB200_ENGINE_TCGEN05) fold = tc_prepare(ws, x, cfg.ldx, n, d, norms, U, thr, tc_sym, s);
 
@@ -618,7 +632,8 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
                          (pl.diag || pl.ndelta <= kSimtRoundMaxOffsets))
                             ? FDB200_ENGINE_SIMT
                             : engine;
-            pl.rows_only = (pl.engine == FDB200_ENGINE_SIMT && engine == FDB200_ENGINE_TCGEN05 && nb < T) ? 1 : 0;
+            pl.rows_only =
+                (pl.engine == FDB200_ENGINE_SIMT && engine == FDB200_ENGINE_TCGEN05 && nb < T && !hooked) ? 1 : 0;
             if (pl.rows_only && !pl.diag) pl.units = 2 * nb * pl.ndelta;
             plan.push_back(pl);
             const int slot = (int)plan.size();
@@ -630,10 +645,13 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
             FDB_CUDA(cudaEventRecord(ev.get(2 * slot), s));
             launch_tile_round(r, pl.units, pl.engine, cfg.precision, s);
             FDB_CUDA(cudaEventRecord(ev.get(2 * slot + 1), s));
+            // symmetric shards: the round's overflow tag and error code are combined (MAX) before the
+            // merge, so every shard discards an overflowed round and re-plans it alike
+            if (hooked) cfg.round_hook(cfg.round_hook_ctx, FDB200_HOOK_FLAGS, ovf, 2, (void*)s);
             if (trace) FDB_CUDA(cudaEventRecord(m0, s));
-            // a sharded tcgen05 round or a rows-only round appends only to this shard's rows; a symmetric
-            // round (SIMT, or tcgen05 over the whole triangle) to any point
-            const bool own_rows = pl.engine == FDB200_ENGINE_TCGEN05 || pl.rows_only;
+            // an ordered tcgen05 round (a shard without a hook) or a rows-only round appends only to this
+            // shard's rows; a symmetric round (SIMT or tcgen05) to any point
+            const bool own_rows = (pl.engine == FDB200_ENGINE_TCGEN05 && !tc_sym) || pl.rows_only;
             const int plo = own_rows ? b_lo * kBlock : 0;
             const int phi = own_rows ? std::min(n, b_hi * kBlock) : n;
             if (k <= kSortedMergeMaxK && cap <= 512)
@@ -643,6 +661,14 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
                 knn_merge_kernel<<<(phi - plo + mwarps - 1) / mwarps, mwarps * 32, msmem, s>>>(
                     lists, thr, U, norms, cand, cnt, plo, phi, k, cap, pw, d, kp, exact, admitted, fold.aimg, fold.ntf, fold.sym, ovf);
             FDB_LAUNCHED();
+            if (hooked) {
+                // every shard's k-th key bounds the union's: filter with the smallest (unsigned MIN)
+                cfg.round_hook(cfg.round_hook_ctx, FDB200_HOOK_THRESHOLDS, thr, n, (void*)s);
+                if (fold.sym) {
+                    refresh_bounds_kernel<<<(n + 255) / 256, 256, 0, s>>>(thr, norms, U, n, d, kp, exact);
+                    FDB_LAUNCHED();
+                }
+            }
             if (trace) FDB_CUDA(cudaEventRecord(m1, s));
             if (!diag_done) {
                 diag_done = true;

@@ -1202,7 +1202,6 @@ void launch_tile_round_tc(const TileRound& r, int units, int precision, cudaStre
     a.cap = r.cap;
     a.exact = precision == FDB200_FP32 ? 1 : 0;
     FDB_REQUIRE(r.sym == st.sym, "tcgen05 round and operand images disagree on the schedule");
-    FDB_REQUIRE(!r.sym || r.nb == r.T, "the symmetric tcgen05 schedule covers the whole triangle");
     a.U = st.U;
     a.nrm = st.nrm;
     a.thr = st.thr;

@@ -5,9 +5,9 @@
 // A round covers the block offsets [delta0, delta0 + ndelta) of T blocks of 128 points. A tile is one
 // row block X against two adjacent column blocks (Y, Y + 1) = (X + delta, X + delta + 1) (mod T); a work
 // item keeps (Y, Y + 1) and walks up to ppi such offset pairs, i.e. the row blocks X = Y - delta.
-//   symmetric (the whole triangle, nb == T): forward offsets only, so each unordered block pair is
-//     covered once; with an even T the offset T/2 reaches {X, X + T/2} from both blocks, and only
-//     X < T/2 keeps it.
+//   symmetric: forward offsets only, so each unordered block pair is covered once (by the shard that
+//     owns its first block, X); with an even T the offset T/2 reaches {X, X + T/2} from both blocks,
+//     and only X < T/2 keeps it.
 //   ordered (a shard of row blocks [b_lo, b_lo + nb)): the offsets and their mirrors T - delta, so each
 //     ordered pair of a shard row block is covered once; T/2 once.
 //   diagonal round: item b is the tile (b_lo + b, b_lo + b), column half 0 only.
@@ -70,7 +70,7 @@ inline void plan_schedule(Sched& a, int T, int diag, int sym, int b_lo, int nb, 
         a.r0[0] = delta0;
         a.len[0] = ndelta;
         a.np[0] = (ndelta + 1) / 2;
-        pairs = (long long)T * a.np[0];
+        pairs = (long long)nb * a.np[0];
     } else {
         // forward offsets [d0, d0 + L) and their mirrors T - delta, the offset T/2 only once
         const int e = ((T & 1) == 0 && delta0 + ndelta - 1 == T / 2) ? 1 : 0;
@@ -88,15 +88,10 @@ inline void plan_schedule(Sched& a, int T, int diag, int sym, int b_lo, int nb, 
     if (ppi > kMaxItemPairs) ppi = kMaxItemPairs;
     a.ppi = sched_min((int)ppi, a.np[0] > 1 ? a.np[0] : 1);
     a.nchunk0 = (a.np[0] + a.ppi - 1) / a.ppi;
-    if (sym) {
-        a.ywin = T;
-        a.items = T * a.nchunk0;
-    } else {
-        // a shard's rows X in [b_lo, b_lo + nb) meet, for one chunk of ppi offset pairs, the column
-        // blocks Y = X + delta: a window of nb + 2 ppi - 1 blocks (all T when unsharded)
-        a.ywin = (nb == T) ? T : sched_min(T, nb + 2 * a.ppi - 1);
-        a.items = a.ywin * (a.nchunk0 + (a.np[1] + a.ppi - 1) / a.ppi);
-    }
+    // a shard's rows X in [b_lo, b_lo + nb) meet, for one chunk of ppi offset pairs, the column blocks
+    // Y = X + delta: a window of nb + 2 ppi - 1 blocks (all T when unsharded)
+    a.ywin = (nb == T) ? T : sched_min(T, nb + 2 * a.ppi - 1);
+    a.items = a.ywin * (a.nchunk0 + (sym ? 0 : (a.np[1] + a.ppi - 1) / a.ppi));
 }
 
 // Work item -> (offset range rho, resident column block Y, its pair indices [p_lo, p_lo + count)).

@@ -39,13 +39,21 @@ class FastDecError(RuntimeError):
         self.code = code
 
 
+# fdb200_round_hook(ctx, kind, dev_ptr, count, stream): kind HOOK_FLAGS = int32 flags to combine by MAX,
+# HOOK_THRESHOLDS = packed uint64 keys to combine by unsigned MIN, over all shards, on `stream`
+ROUND_HOOK = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_longlong,
+                              ctypes.c_void_p)
+HOOK_FLAGS, HOOK_THRESHOLDS = 0, 1
+
+
 class Opts(ctypes.Structure):
     _fields_ = [("struct_size", ctypes.c_int), ("device", ctypes.c_int), ("precision", ctypes.c_int),
                 ("density_kernel", ctypes.c_int), ("engine", ctypes.c_int),
                 ("inputs_on_device", ctypes.c_int), ("outputs_on_device", ctypes.c_int),
                 ("shard_rank", ctypes.c_int), ("shard_count", ctypes.c_int),
                 ("cand_capacity", ctypes.c_int), ("stream", ctypes.c_void_p),
-                ("shard_block_lo", ctypes.c_int), ("shard_block_hi", ctypes.c_int)]
+                ("shard_block_lo", ctypes.c_int), ("shard_block_hi", ctypes.c_int),
+                ("round_hook", ROUND_HOOK), ("round_hook_ctx", ctypes.c_void_p)]
 
 
 class Stats(ctypes.Structure):
@@ -122,7 +130,7 @@ _CUDA_STREAM_LEGACY = 0x1   # cudaStreamLegacy
 
 
 def make_opts(device=0, precision="fp32", density="laplacian", engine="auto", on_device=False,
-              shard=(0, 1), cand_capacity=0, stream=None, blocks=None):
+              shard=(0, 1), cand_capacity=0, stream=None, blocks=None, round_hook=None):
     o = Opts()
     lib().fdb200_opts_init(ctypes.byref(o))
     o.device = int(device)
@@ -134,6 +142,8 @@ def make_opts(device=0, precision="fp32", density="laplacian", engine="auto", on
     o.cand_capacity = int(cand_capacity)
     if blocks is not None:   # explicit shard: row blocks [blocks[0], blocks[1])
         o.shard_block_lo, o.shard_block_hi = int(blocks[0]), int(blocks[1])
+    if round_hook is not None:   # a ROUND_HOOK; the caller keeps it alive for the call
+        o.round_hook = round_hook
     # stream: None = the library's own stream; an integer handle runs the call on that CUDA stream.
     # Handle 0 is the legacy default stream (torch's default stream reports 0); the ABI reserves a
     # NULL stream for "the library's own", so it is passed as cudaStreamLegacy.

@@ -2,10 +2,19 @@
 by points.
 
 The reference is single-GPU (its sources use no NCCL or MPI). Here every rank evaluates the block pairs
-of its share of the triangle (fdb200_knn_partial on its row blocks). With the tcgen05 engine and the
-automatic engine (whose dense first rounds run on rows-only SIMT tiles when sharded) a rank tests its
-own rows against every column block, so the lists of its own points are final when its rounds end;
-rank 0 gathers them. With the SIMT engine a rank's symmetric tiles update points of every rank, so its
+of its share of the triangle (fdb200_knn_partial on its row blocks), in one of two ways:
+  ordered shards (`sym_shards=False`, or FASTDEC_SYM_SHARDS=0): with the tcgen05 engine and the
+    automatic engine (whose dense first rounds run on rows-only SIMT tiles when sharded) a rank tests
+    its own rows against every column block, so the lists of its own points are final when its rounds
+    end; rank 0 gathers them.
+  symmetric shards (the default with the tcgen05 and automatic engines): a rank multiplies only the block pairs
+    whose first block is its own, once, and tests both endpoints, as the one-GPU schedule does, so the
+    shards together do half the tensor work. Its tiles then update points of every rank: after every
+    round the library calls back (`round_hook`) and the ranks combine the round's overflow flags (MAX,
+    so an overflowed round is discarded and re-planned alike everywhere) and every point's threshold
+    (unsigned MIN of the packed keys: each rank's k-th key bounds the union's, so each rank filters with
+    the tightest). At the end the partial lists go to their owners as below.
+With the SIMT engine (and with symmetric shards) a rank's tiles update points of every rank, so its
 partial lists go to their owners with one all-to-all and the owners merge them (the lexicographic
 (d2, index) k-smallest is associative and commutative, so the merged lists equal the single-GPU ones).
 
@@ -116,10 +125,49 @@ def all_reduce_keys_min(best: torch.Tensor):
     best.copy_(keys_to_signed(s))
 
 
+class _DeviceArray:
+    """CUDA array interface over `count` elements at a device pointer of the library (no copy)"""
+
+    def __init__(self, ptr, count, typestr):
+        self.__cuda_array_interface__ = {"shape": (int(count),), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 2}
+
+
+class RoundHook:
+    """The symmetric shards' round hook: combines the library's per-round flags (MAX) and per-point
+    thresholds (unsigned MIN) over all ranks with torch.distributed, on the current stream (which is
+    the stream the library runs on). Errors inside the callback are kept and raised after the call."""
+
+    def __init__(self, device):
+        import fastdec_b200 as fdb
+        self.device = device
+        self.errors = []
+        self.calls = 0
+        self.flags_kind = fdb.HOOK_FLAGS
+        self.c_hook = fdb.ROUND_HOOK(self._hook)
+
+    def _hook(self, ctx, kind, ptr, count, stream):
+        try:
+            self.calls += 1
+            if kind == self.flags_kind:
+                t = torch.as_tensor(_DeviceArray(ptr, count, "<i4"), device=self.device)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            else:
+                t = torch.as_tensor(_DeviceArray(ptr, count, "<i8"), device=self.device)
+                all_reduce_keys_min(t)
+        except Exception as e:   # an exception cannot cross the C call; raise it after the call returns
+            self.errors.append(e)
+
+    def check(self):
+        if self.errors:
+            err, self.errors = self.errors[0], []
+            raise RuntimeError(f"round hook failed: {err!r}")
+
+
 class ShardedFit:
     """One fit across `world` GPUs (see the module docstring). step() returns rank-local stats."""
 
-    def __init__(self, n, d, k, c, rank, world, device, stream_ptr, rank0_share=None, **opts):
+    def __init__(self, n, d, k, c, rank, world, device, stream_ptr, rank0_share=None, sym_shards=None, **opts):
         import fastdec_b200 as fdb
         self.fdb = fdb
         self.n, self.d, self.k, self.c = n, d, k, c
@@ -129,6 +177,10 @@ class ShardedFit:
         if rank0_share is None:
             rank0_share = float(os.environ.get("FASTDEC_RANK0_SHARE", "1.0"))
         self.set_rank0_share(rank0_share)
+        if sym_shards is None:
+            sym_shards = os.environ.get("FASTDEC_SYM_SHARDS", "1") == "1"
+        self.sym = bool(sym_shards) and world > 1 and opts.get("engine", "auto") != "simt"
+        self.hook = RoundHook(device) if self.sym else None
         self.lists = torch.empty((n, k), dtype=torch.int64, device=device)
         if rank == 0:
             self.dist = torch.empty((k, n), dtype=torch.float32, device=device)
@@ -147,10 +199,13 @@ class ShardedFit:
     def step(self, x_dev, centers, labels):
         fdb, n, k, c, rank, world, sp = self.fdb, self.n, self.k, self.c, self.rank, self.world, self.sp
         _log(rank, "step: partial kNN")
+        hook = {"round_hook": self.hook.c_hook} if self.sym else {}
         st = fdb.knn_partial_device(x_dev, k, self.lists, (rank, world), stream=sp, blocks=self.blocks[rank],
-                                    **self.opts)
+                                    **hook, **self.opts)
+        if self.sym:
+            self.hook.check()
         n_own = 0
-        if st.get("engine_used") == 2:
+        if st.get("engine_used") == 2 and not self.sym:
             # rows-only schedule: this rank's block rows are final, nothing to exchange or merge
             a, b = self.ranges[rank]
             _log(rank, "step: gather")

@@ -6,6 +6,8 @@
 //     exactly one tile column half over all rounds, and the diagonal round covers each block once;
 //   * the ordered schedule of a shard: every ordered pair (X, Y) with X in the shard's row blocks is
 //     covered exactly once (X = Y by the diagonal round), and no other row block is ever covered;
+//   * the symmetric schedule split over 2, 3 or 8 shards: the shards' tiles together cover every
+//     unordered pair exactly once, and each shard's tiles have their row block in the shard;
 //   * item_tiles (the MMA issuer's count) equals the number of pairs tile_of accepts in every item;
 //   * every tile's row block lies in the shard and its column blocks in [0, T).
 // Prints "ok <cases>" or the first failure, and exits non-zero on a failure.
@@ -49,22 +51,63 @@ static int walk(const Sched& s, std::vector<int>& cov, int ctas)
     return 0;
 }
 
-// one fit: the diagonal round, then the offsets 1 .. T/2 cut into consecutive rounds
-static int fit(int T, int b_lo, int nb, int sym, int ctas, std::mt19937& rng)
+// the offsets 1 .. T/2 cut into consecutive rounds (delta0, ndelta), as the planner cuts them
+static std::vector<std::pair<int, int>> partition(int T, std::mt19937& rng)
 {
-    std::vector<int> cov((size_t)T * T, 0);
-    Sched s;
-    fdb::tc::plan_schedule(s, T, 1, sym, b_lo, nb, 0, 0, ctas);
-    if (walk(s, cov, ctas)) return 1;
+    std::vector<std::pair<int, int>> r;
     const int dmax = T / 2;
     int d0 = 1;
     while (d0 <= dmax) {
         std::uniform_int_distribution<int> len(1, std::max(1, std::min(dmax - d0 + 1, 1 + (int)(rng() % 600))));
         const int L = std::min(len(rng), dmax - d0 + 1);
-        fdb::tc::plan_schedule(s, T, 0, sym, b_lo, nb, d0, L, ctas);
-        if (walk(s, cov, ctas)) return 1;
+        r.push_back({d0, L});
         d0 += L;
     }
+    return r;
+}
+
+// one shard's fit: the diagonal round, then the rounds of the partition, into cov
+static int cover(int T, int b_lo, int nb, int sym, int ctas, const std::vector<std::pair<int, int>>& rounds,
+                 std::vector<int>& cov)
+{
+    Sched s;
+    fdb::tc::plan_schedule(s, T, 1, sym, b_lo, nb, 0, 0, ctas);
+    if (walk(s, cov, ctas)) return 1;
+    for (const auto& r : rounds) {
+        fdb::tc::plan_schedule(s, T, 0, sym, b_lo, nb, r.first, r.second, ctas);
+        if (walk(s, cov, ctas)) return 1;
+    }
+    return 0;
+}
+
+// symmetric coverage: (X, Y) and (Y, X) together once, the diagonal once
+static int check_unordered(const std::vector<int>& cov, int T, int world, int ctas)
+{
+    for (int X = 0; X < T; ++X)
+        for (int Y = X; Y < T; ++Y) {
+            const int both = X == Y ? cov[(size_t)X * T + X] : cov[(size_t)X * T + Y] + cov[(size_t)Y * T + X];
+            if (both != 1) return fail("symmetric coverage", T, 0, T, 1, ctas, X, Y + 1000000 * world);
+        }
+    return 0;
+}
+
+// the symmetric schedule split over `world` shards of even block ranges
+static int sym_shards(int T, int world, int ctas, std::mt19937& rng)
+{
+    std::vector<int> cov((size_t)T * T, 0);
+    const auto rounds = partition(T, rng);
+    for (int rank = 0; rank < world; ++rank) {
+        const int lo = (int)((long)T * rank / world), hi = (int)((long)T * (rank + 1) / world);
+        if (hi > lo && cover(T, lo, hi - lo, 1, ctas, rounds, cov)) return 1;
+    }
+    return check_unordered(cov, T, world, ctas);
+}
+
+// one fit of one shard (the whole triangle when nb == T)
+static int fit(int T, int b_lo, int nb, int sym, int ctas, std::mt19937& rng)
+{
+    std::vector<int> cov((size_t)T * T, 0);
+    if (cover(T, b_lo, nb, sym, ctas, partition(T, rng), cov)) return 1;
     for (int X = 0; X < T; ++X)
         for (int Y = 0; Y < T; ++Y) {
             const int c = cov[(size_t)X * T + Y];
@@ -100,6 +143,8 @@ int main()
                 ++cases;
                 for (int world : {2, 3, 8}) {
                     if (world > T) continue;
+                    if (sym_shards(T, world, ctas, rng)) return 1;
+                    ++cases;
                     for (int rank = 0; rank < world; ++rank) {
                         const int lo = (int)((long)T * rank / world), hi = (int)((long)T * (rank + 1) / world);
                         if (hi > lo && fit(T, lo, hi - lo, 0, ctas, rng)) return 1;

@@ -38,7 +38,7 @@ def test_opts_init_and_version_need_no_gpu(fdb):
     assert lib.fdb200_opts_init(ctypes.byref(o)) == 0
     assert o.struct_size == ctypes.sizeof(fdb.Opts)
     assert o.shard_count == 1 and o.precision == fdb.FP32
-    assert lib.fdb200_abi_version() == 2
+    assert lib.fdb200_abi_version() == 3
     assert ctypes.sizeof(fdb.Stats) == 8 * 7 + 8 * 2 + 4 * 6 + 4 * 6  # matches FdB200Stats (120 bytes)
 
 

@@ -15,7 +15,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, n, q, engine, share):
+def _rank(rank, world, port, n, q, engine, share, sym, cap):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -33,12 +33,15 @@ def _rank(rank, world, port, n, q, engine, share):
         xd = torch.from_numpy(x).to(dev)
         k, c = 30, 10
         sp = torch.cuda.current_stream(dev).cuda_stream
-        runner = ShardedFit(n, 50, k, c, rank, world, dev, sp, rank0_share=share, engine=engine)
+        runner = ShardedFit(n, 50, k, c, rank, world, dev, sp, rank0_share=share, engine=engine, sym_shards=sym,
+                            cand_capacity=cap)
         centers = torch.empty(c, dtype=torch.int32, device=dev)
         labels = torch.empty(n, dtype=torch.int32, device=dev)
         for _ in range(2):   # twice: buffers and lists are reused across steps
             runner.step(xd, centers, labels)
         torch.cuda.synchronize(dev)
+        if sym and not (runner.hook and runner.hook.calls > 0):
+            raise RuntimeError("symmetric shards ran without their round hook")
         if rank == 0:
             ref = fdb.fit(x, k, c, engine=engine)
             same = (centers.cpu().numpy().tolist() == ref["centers"].tolist()
@@ -54,12 +57,17 @@ def _rank(rank, world, port, n, q, engine, share):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("engine,share", [("auto", 1.0), ("auto", 0.8), ("simt", 1.0)])
-def test_sharded_fit_on_two_gpus_matches_one_gpu(engine, share):
+@pytest.mark.parametrize("engine,share,sym,cap", [("auto", 1.0, False, 0), ("auto", 0.8, False, 0),
+                                                  ("simt", 1.0, False, 0), ("auto", 1.0, True, 0),
+                                                  ("auto", 0.8, True, 0), ("auto", 1.0, True, 256)])
+def test_sharded_fit_on_two_gpus_matches_one_gpu(engine, share, sym, cap):
     """engine auto: rows-only shards (SIMT tiles for the dense rounds, then tcgen05), each rank's rows
     final, gather only; share 0.8 gives rank 0 a smaller share of the triangle. engine simt: symmetric
     tiles, partial lists for every point, the NCCL all-to-all to the owners and fdb200_merge_lists.
-    Either way the DC reduction is sharded over both GPUs."""
+    Symmetric shards (sym): each unordered block pair once over both GPUs, both endpoints tested,
+    thresholds combined after every round through the round hook, partial lists exchanged to their
+    owners; cap 256 makes candidate overflows (re-planned alike on both ranks) likely. Either way the
+    DC reduction is sharded over both GPUs."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -67,7 +75,7 @@ def test_sharded_fit_on_two_gpus_matches_one_gpu(engine, share):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, 150_000 if engine == "auto" else 40_000, q, engine, share)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, 150_000 if engine == "auto" else 40_000, q, engine, share, sym, cap)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in range(2))
