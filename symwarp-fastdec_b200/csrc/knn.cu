@@ -603,7 +603,9 @@ KnnResult knn_lists(Workspace& ws, const float* x, const KnnConfig& cfg, cudaStr
     int pending = 0;            // block offsets of a round being re-planned, 0 = none
     cudaEvent_t m0 = ev.get(0), m1 = ev.get(1);   // trace: merge timing
     for (;;) {
-        const bool more = nb > 0 && (!diag_done || next_delta <= dmax);
+        // with a round hook every shard plans the same rounds, even an empty one (its launches do no
+        // work), so that every shard makes the same hook calls
+        const bool more = (nb > 0 || hooked) && (!diag_done || next_delta <= dmax);
         if (more) {
             Planned pl{};
             pl.seen = seen;

@@ -146,15 +146,18 @@ class RoundHook:
         self.flags_kind = fdb.HOOK_FLAGS
         self.c_hook = fdb.ROUND_HOOK(self._hook)
 
+    def combine(self, kind, t: torch.Tensor):
+        """in place over all ranks: int32 flags by MAX, packed uint64 keys (held in int64) by unsigned MIN"""
+        if kind == self.flags_kind:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        else:
+            all_reduce_keys_min(t)
+
     def _hook(self, ctx, kind, ptr, count, stream):
         try:
             self.calls += 1
-            if kind == self.flags_kind:
-                t = torch.as_tensor(_DeviceArray(ptr, count, "<i4"), device=self.device)
-                dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            else:
-                t = torch.as_tensor(_DeviceArray(ptr, count, "<i8"), device=self.device)
-                all_reduce_keys_min(t)
+            typestr = "<i4" if kind == self.flags_kind else "<i8"
+            self.combine(kind, torch.as_tensor(_DeviceArray(ptr, count, typestr), device=self.device))
         except Exception as e:   # an exception cannot cross the C call; raise it after the call returns
             self.errors.append(e)
 

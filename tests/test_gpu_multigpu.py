@@ -15,7 +15,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, n, q, engine, share, sym, cap):
+def _rank(rank, world, port, n, q, engine, share, sym, cap, c=10):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -31,7 +31,7 @@ def _rank(rank, world, port, n, q, engine, share, sym, cap):
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
         x = embedding_cloud(n=n, d=50, seed=5)
         xd = torch.from_numpy(x).to(dev)
-        k, c = 30, 10
+        k = 30
         sp = torch.cuda.current_stream(dev).cuda_stream
         runner = ShardedFit(n, 50, k, c, rank, world, dev, sp, rank0_share=share, engine=engine, sym_shards=sym,
                             cand_capacity=cap)
@@ -76,6 +76,29 @@ def test_sharded_fit_on_two_gpus_matches_one_gpu(engine, share, sym, cap):
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_rank, args=(r, 2, port, 150_000 if engine == "auto" else 40_000, q, engine, share, sym, cap)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+    assert results == {0: "ok", 1: "ok"}
+
+
+@pytest.mark.gpu
+def test_symmetric_shards_with_an_empty_shard_match_one_gpu():
+    """300 points are 3 blocks of 128: with rank0_share 0.1 rank 0 gets no row blocks at all, yet under
+    symmetric shards it must still make every round-hook call the other rank makes (or that rank's
+    collectives would wait for it) and take part in the exchange; the fit equals the one-GPU fit."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from fastdec_b200.multigpu import block_split
+    assert block_split(300, 2, 0.1)[0] == (0, 0)
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, 300, q, "auto", 0.1, True, 0, 3)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in range(2))

@@ -235,3 +235,50 @@ def test_dc_partial_keys_combine_by_unsigned_min_over_ranks():
     for p in procs:
         p.join(timeout=60)
     assert results == {r: "ok" for r in range(world)}
+
+
+def _round_hook_worker(rank, world, port, q):
+    import fastdec_b200 as fdb
+    from fastdec_b200.multigpu import RoundHook
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        hook = RoundHook(torch.device("cpu"))
+        # flags: overflow tag and error code, combined by MAX (rank 1 overflowed in round 3)
+        flags = torch.tensor([3 if rank == 1 else 0, 0], dtype=torch.int32)
+        hook.combine(fdb.HOOK_FLAGS, flags)
+        assert flags.tolist() == [3, 0]
+        # thresholds: packed keys, unsigned MIN; an empty list's key (UINT64_MAX) loses to any real key
+        rng = np.random.default_rng(11)
+        parts = []
+        for s in range(world):
+            d2 = np.abs(rng.standard_normal(500)).astype(np.float32)
+            k = (d2.view(np.uint32).astype(np.uint64) << np.uint64(32)) | rng.integers(0, 10 ** 6, 500).astype(np.uint64)
+            k[rng.random(500) < 0.2] = EMPTY
+            parts.append(k)
+        mine = torch.from_numpy(parts[rank].view(np.int64).copy())
+        hook.combine(fdb.HOOK_THRESHOLDS, mine)
+        assert np.array_equal(mine.numpy().view(np.uint64), np.minimum.reduce(parts))
+        q.put((rank, "ok"))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_round_hook_combines_flags_by_max_and_thresholds_by_unsigned_min():
+    """The symmetric shards' round hook: the round's flags combine by MAX (so every rank sees an
+    overflow any rank had), the per-point thresholds by unsigned MIN of the packed keys (each rank's
+    k-th key bounds the union's; UINT64_MAX = a list not yet full)."""
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_round_hook_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert results == {r: "ok" for r in range(world)}
