@@ -121,12 +121,20 @@ def pairs_of(n):
     return n * (n - 1) // 2
 
 
+def parallelism_of(a):
+    """how the triangle is split: one GPU, or shards (symmetric by default, FASTDEC_SYM_SHARDS=0: ordered)"""
+    if a.gpus <= 1:
+        return "triangle-sharded x1"
+    ordered = os.environ.get("FASTDEC_SYM_SHARDS", "1") != "1" or a.engine == "simt"
+    return f"triangle-sharded x{a.gpus}, {'ordered' if ordered else 'symmetric'} shards"
+
+
 def config_of(a, extra=None):
     mb = lambda b: f"{b / 1e6:,.0f} MB"
     c = {"workload": f"{a.config} {a.n:,} x {a.d}, k={a.k}, c={a.c}, {a.precision.upper()} distances, "
                      f"{a.density} density",
          "n": a.n, "d": a.d, "k": a.k, "c": a.c, "precision": a.precision, "density": a.density,
-         "engine": a.engine, "seed": a.seed, "parallelism": f"triangle-sharded x{a.gpus}",
+         "engine": a.engine, "seed": a.seed, "parallelism": parallelism_of(a),
          "l2": f"inputs larger than L2 ({mb(4 * a.n * a.d)} dataset, {mb(8 * a.n * a.k)} lists per fit; "
                "no flush needed)" if 8 * a.n * a.k > 126e6 else "inputs smaller than L2 (not flushed)"}
     if extra:
