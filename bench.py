@@ -520,7 +520,6 @@ def main():
     if rank != 0:
         return 0
 
-    bf16, hbm, src = measured_peaks()
     tf32_peak = TF32_PEAK["tflops_sustained"]
     flops = shard_pairs * 2 * d
     achieved = flops / (tile_ms / 1e3) / 1e12 if tile_ms > 0 else None
