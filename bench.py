@@ -237,15 +237,6 @@ def measure_tf32_peak(seconds=4.0, size=8192):
             "gpu_name": torch.cuda.get_device_name(dev)}
 
 
-def measured_peaks():
-    """(bf16 TF/s for a kernel timed inside a long loop, i.e. the sustained figure, HBM GB/s, source)"""
-    p = ROOT / "MEASURED_PEAKS.json"
-    if p.exists():
-        j = json.loads(p.read_text())
-        return j.get("bf16_tflops_sustained", j.get("bf16_tflops", 1590.0)), j.get("hbm_gbs", 6650.0), "measured"
-    return 1400.0, 6650.0, "fallback"
-
-
 # ------------------------------------------------------------------ CPU reference (oracle/_ref)
 def run_reference_sample(x_full, a, target_s, steps=1, warmup=0):
     """Times the reference's host Fit (oracle/_ref) on a prefix sample of the (shuffled) dataset."""
