@@ -81,7 +81,8 @@ typedef struct FdB200Opts {
                                  cudaStreamLegacy to run on the legacy default stream) */
     int shard_block_lo;       /* explicit shard: the 128-point row blocks [shard_block_lo, shard_block_hi) */
     int shard_block_hi;       /* (-1, -1 = the even split given by shard_rank / shard_count) */
-    fdb200_round_hook round_hook;   /* fdb200_knn_partial: NULL = ordered shards (each shard's rows
+    fdb200_round_hook round_hook;   /* fdb200_knn_partial only (other calls ignore it): NULL =
+                                       ordered shards (each shard's rows
                                        against every column, its own lists final, no exchange);
                                        set = symmetric shards (each unordered block pair once over all
                                        shards, partial lists of every point, thresholds combined

@@ -51,6 +51,14 @@ KnnConfig knn_config(int n, int d, int k, const FdB200Opts& o)
     c.cand_capacity = o.cand_capacity;
     c.block_lo = o.shard_block_lo;
     c.block_hi = o.shard_block_hi;
+    return c;
+}
+
+// the configuration of fdb200_knn_partial: as above, plus the symmetric shards' round hook (the other
+// entry points run the whole triangle on one device and ignore it)
+KnnConfig knn_partial_config(int n, int d, int k, const FdB200Opts& o)
+{
+    KnnConfig c = knn_config(n, d, k, o);
     c.round_hook = o.round_hook;
     c.round_hook_ctx = o.round_hook_ctx;
     return c;
@@ -399,7 +407,7 @@ int fdb200_knn_partial(const float* data_dev, int n, int d, int k, const FdB200O
         FDB_REQUIRE(data_dev && lists_dev, "fdb200_knn_partial: null pointer");
         StageTimer tm(s);
         const int a = tm.mark();
-        KnnResult r = knn_lists(ws, data_dev, knn_config(n, d, k, o), s);
+        KnnResult r = knn_lists(ws, data_dev, knn_partial_config(n, d, k, o), s);
         FDB_CUDA(cudaMemcpyAsync(lists_dev, r.lists, sizeof(uint64_t) * (size_t)n * k, cudaMemcpyDeviceToDevice, s));
         const int b = tm.mark();
         FDB_CUDA(cudaStreamSynchronize(s));
