@@ -516,6 +516,7 @@ def main():
     achieved = flops / (tile_ms / 1e3) / 1e12 if tile_ms > 0 else None
     default_shape = vs_baseline(a, 1.0) is not None and (world, a.precision, a.engine) == (1, "fp32", "auto")
     kp = ((d + 6 + 7) // 8) * 8
+    pairs_once = world == 1 or bool(runner.sym)   # symmetric schedule: every unordered pair multiplied once
     roofline = {"bound": "tensor", "kernel": "distance tiles (knn_tile_simt for the dense first rounds + knn_tile_tc, all rounds of a fit)",
                 "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
                 "frac": (achieved / tf32_peak) if achieved else None,
@@ -526,12 +527,12 @@ def main():
                              f"the seconds-long timed loop; of measured",
                 "launches_per_fit": rounds, "algorithmic_flops_per_fit": flops,
                 "algorithmic_note": "N(N-1)/2 pairs x 2d FLOPs (the reference's -2 X X^T GEMM work)",
-                "tensor_flops_per_fit": (float(n) * n * kp * (1 if world == 1 else 2)
+                "tensor_flops_per_fit": (float(n) * n * kp * (1 if pairs_once else 2)
                                          if engine_name(stats) == "tcgen05" else None),
-                "tensor_note": "upper bound of what the tcgen05 pipe executes, K = d + 6 padded to 8: one GPU runs "
-                                "the symmetric schedule (every unordered pair once), a shard ordered pairs over its "
-                                "rows (every pair twice across the shards); the first rounds, which the automatic "
-                                "engine gives the SIMT tiles, cover 0.4 % of the pairs at the headline shape"}
+                "tensor_note": "upper bound of what the tcgen05 pipe executes, K = d + 6 padded to 8: one GPU and "
+                                "symmetric shards run the symmetric schedule (every unordered pair once), ordered "
+                                "shards every pair twice; the first rounds, which the automatic engine gives the "
+                                "SIMT tiles, cover 0.4 % of the pairs at the headline shape"}
     last = stats[-1]
     out = {"metric": "fit_distance_pairs_per_s", "value": value, "unit": "pairs/s", "n_gpus": world,
            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
